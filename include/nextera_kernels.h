@@ -1,0 +1,116 @@
+/* nextera_kernels.h -- the thin C-ABI kernel layer of libnexterabert.so (sm_100a).
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (cudaStream_t passed as void *; NULL = the legacy default stream) and only
+ * enqueues work: nothing here synchronises or allocates unless it says so.
+ * The host library (nexterabert.h) is built on these; tests and benchmarks call
+ * them directly to check one kernel at a time.  Each function names the
+ * reference routine (src/nexterabert.cpp of Rikka-Botan/NexteraBERT.cpp) whose
+ * results it reproduces.
+ *
+ * Data layouts (row t of a [T][C] tensor starts at t * C):
+ *   fp32 activations  [T][C]
+ *   int8 activations  q [T][C] as s8 codes (the reference's u8 code minus 128)
+ *                     sx [T][n_blk] fp32, n_blk = ceil(C / 256)
+ *   int8 weights      w [N][K] s8, sw [n_blk][N] fp32 (off [n_blk][N] int32 optional)
+ *   attention         q [T][H*D] row-major, k / v head-major [G][T][D]
+ *   documents         doc_start[n_docs], doc_len[n_docs], row_doc[T]
+ *
+ * Return value: 0 on success, NXK_EINVAL for arguments the kernels do not
+ * support, NXK_ELAUNCH when the launch itself failed.  Kernels that wait on
+ * a pipeline report a timed-out wait through nxk_take_error().
+ */
+#ifndef NEXTERA_KERNELS_H
+#define NEXTERA_KERNELS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "nexterabert.h"   /* NEXTERA_API */
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NXK_OK       0
+#define NXK_EINVAL  (-1)
+#define NXK_ELAUNCH (-2)
+
+/* device-side error word of the current device: returns it and clears it
+ * (synchronises the stream).  Nonzero = a kernel gave up on a bounded wait. */
+NEXTERA_API int32_t nxk_take_error(void * stream);
+
+/* ---- weights: build_i8_weight (:1010-1049), on the device ----
+ * blocks: n_out rows of GGUF blocks of `type` (any of F32 F16 BF16 Q4_0 Q4_1
+ * Q5_0 Q5_1 Q8_0 Q2_K Q3_K Q4_K Q5_K Q6_K); writes w8, scale and (if not NULL) off. */
+NEXTERA_API int nxk_expand_weight(int type, const void * blocks, int n_in, int n_out,
+                                  int8_t * w8, float * scale, int32_t * off, void * stream);
+
+/* ---- embedding: ggml_get_rows (+ ggml_add of segment rows), :1272-1273 ----
+ * table: n_rows rows of C values in blocks of `type`.  An id outside [0, n_rows)
+ * yields a zero row and sets the device error word (ids are checked on the host
+ * before host-memory calls; device-resident ids are checked here). */
+NEXTERA_API int nxk_embed(int type, const void * table, int n_rows, int C, const int32_t * tokens, int T,
+                          int ttype, const void * ttable, int tn_rows, const int32_t * types, float * out,
+                          void * stream);
+
+/* ---- int8 linear: op_linear_i8 (:969-1007) ----
+ * out[t][n] = (res[t][n] +) sum_B fma(float(S_B) * sx[t][B], sw[B][n], .), S_B the
+ * int32 dot product of block B.  tcgen05 kind::i8 kernel; res may be NULL. */
+NEXTERA_API int nxk_linear_i8(const int8_t * xq, const float * sx, int T, const int8_t * w8, const float * sw,
+                              int K, int N, const float * res, float * out, void * stream);
+/* the same result from a plain CUDA-core kernel (validation only) */
+NEXTERA_API int nxk_linear_i8_simt(const int8_t * xq, const float * sx, int T, const int8_t * w8, const float * sw,
+                                   int K, int N, const float * res, float * out, void * stream);
+/* int32 block sums S_B, [T][N][n_blk] (validation of the integer path) */
+NEXTERA_API int nxk_block_sums(const int8_t * xq, int T, const int8_t * w8, int K, int N, int32_t * sums, void * stream);
+
+/* ---- row ops (:453-690).  q / sx NULL: fp32 `out`; otherwise int8 output ---- */
+NEXTERA_API int nxk_quantize(const float * x, int T, int C, int8_t * q, float * sx, void * stream);
+NEXTERA_API int nxk_rms_norm(const float * x, const float * gain, float eps, int T, int C,
+                             float * out, int8_t * q, float * sx, void * stream);
+NEXTERA_API int nxk_relu_sqr(const float * x, int T, int C, float * out, int8_t * q, float * sx, void * stream);
+NEXTERA_API int nxk_gate(const float * g, const float * y, int T, int C, float * out, int8_t * q, float * sx,
+                         void * stream);
+NEXTERA_API int nxk_dwconv(const float * x, const float * r, const float * taps, int k,
+                           const int32_t * row_doc, const int32_t * doc_start, const int32_t * doc_len,
+                           int T, int C, float * out, int8_t * q, float * sx, void * stream);
+NEXTERA_API int nxk_lily_state(const float * a, const float * x, const float * b, const float * taps, int k,
+                               const int32_t * row_doc, const int32_t * doc_start, const int32_t * doc_len,
+                               int T, int C, float * out, int8_t * q, float * sx, void * stream);
+NEXTERA_API int nxk_qk_prep(const float * x, const float * alpha, const float * beta,
+                            const float * cos_t, const float * sin_t, const int32_t * row_doc,
+                            const int32_t * doc_start, int T, int H, int D, int head_major, float * out,
+                            void * stream);
+NEXTERA_API int nxk_head_major(const float * x, int T, int H, int D, float * out, void * stream);
+NEXTERA_API int nxk_block_mean(const float * h, const float * g, int C, int block,
+                               const int32_t * doc_start, const int32_t * doc_len,
+                               const int32_t * bdoc_start, const int32_t * brow_doc, int n_brows,
+                               float * out, int8_t * q, float * sx, void * stream);
+NEXTERA_API int nxk_upsample_add(const float * y, const float * r, int C, int block, int T,
+                                 const int32_t * row_doc, const int32_t * doc_start, const int32_t * bdoc_start,
+                                 float * out, void * stream);
+/* ggml_norm * w + b (:1292-1293); w / b may be NULL */
+NEXTERA_API int nxk_layer_norm(const float * x, const float * w, const float * b, float eps, int T, int C,
+                               float * out, void * stream);
+/* run_forward's pooling (:1903-1918): per-document sum, then 1/n or 1/||sum|| */
+NEXTERA_API int nxk_pool(const float * hidden, const int32_t * doc_start, const int32_t * doc_len, int n_docs,
+                         int C, int normalize, float * pooled, void * stream);
+
+/* ---- attention: op_attention (:785-852), varlen GQA over packed documents ----
+ * half < 0: full attention inside each document, else the band |i - j| <= half.
+ * scale[n_docs] on the device.  h_doc_start / h_doc_len: the same layout in host
+ * memory, used to plan the work; the plan (nxk_attention_workspace bytes) is
+ * written to `workspace` on the device. */
+NEXTERA_API size_t nxk_attention_workspace(const int32_t * h_doc_len, int n_docs, int half);
+NEXTERA_API int nxk_attention(const float * q, const float * k, const float * v, int T, int H, int G, int D,
+                              int half, const float * scale, const int32_t * row_doc,
+                              const int32_t * doc_start, const int32_t * doc_len, int n_docs,
+                              const int32_t * h_doc_start, const int32_t * h_doc_len,
+                              void * workspace, size_t workspace_bytes, float * out, void * stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

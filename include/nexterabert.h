@@ -1,0 +1,138 @@
+/* nexterabert.h -- public C API of libnexterabert.so, the B200 (sm_100a) build.
+ *
+ * Drop-in for the reference runtime's API (Rikka-Botan/NexteraBERT.cpp,
+ * src/nexterabert.h:28-123): the same functions, argument meanings, return codes
+ * and ownership rules, so tools/cli.cpp and python/nexterabert_cpp.py of the
+ * reference run unchanged against this library.  The function names, the
+ * nextera_params layout and the NEXTERA_API visibility macro must stay
+ * identical to the reference's for that reason; the comments below describe
+ * this implementation.
+ *
+ * Execution model: nextera_load expands every quantized linear weight to int8
+ * on the current CUDA device; each call then runs the whole encoder on that
+ * device and copies results to the caller's host arrays before returning.
+ * One call at a time per context.
+ */
+#ifndef NEXTERABERT_H
+#define NEXTERABERT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(NEXTERA_SHARED)
+#  if defined(_WIN32)
+#    if defined(NEXTERA_BUILD)
+#      define NEXTERA_API __declspec(dllexport)
+#    else
+#      define NEXTERA_API __declspec(dllimport)
+#    endif
+#  else
+#    define NEXTERA_API __attribute__((visibility("default")))
+#  endif
+#else
+#  define NEXTERA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+struct nextera_context;
+
+/* reference: src/nexterabert.h:30-36 */
+struct nextera_params {
+    int32_t n_threads;   /* host threads for load-time work; <= 0: all cores */
+    int32_t use_int8;    /* accepted for compatibility; linear layers always run int8 on the GPU */
+    int32_t use_repack;  /* accepted for compatibility; no effect */
+    int32_t verbosity;   /* 0 silent, 1 load summary on stderr */
+};
+
+/* reference: src/nexterabert.h:38 */
+NEXTERA_API struct nextera_params nextera_default_params(void);
+
+/* Loads a nexterabert GGUF onto the current CUDA device.  NULL on failure, with
+ * the reason on stderr (bad file, unsupported tensor type, no CUDA device).
+ * reference: src/nexterabert.h:40-42 */
+NEXTERA_API struct nextera_context * nextera_load(const char * path, struct nextera_params params);
+NEXTERA_API void nextera_free(struct nextera_context * ctx);
+
+/* model facts (reference: src/nexterabert.h:44-66) */
+NEXTERA_API int32_t nextera_n_embd(const struct nextera_context * ctx);
+NEXTERA_API int32_t nextera_n_vocab(const struct nextera_context * ctx);
+NEXTERA_API int32_t nextera_n_layer(const struct nextera_context * ctx);
+NEXTERA_API int32_t nextera_has_mlm_head(const struct nextera_context * ctx);
+NEXTERA_API int32_t nextera_has_pooler(const struct nextera_context * ctx);
+NEXTERA_API int32_t nextera_n_token_types(const struct nextera_context * ctx);
+NEXTERA_API const char * nextera_classifier_task(const struct nextera_context * ctx);
+NEXTERA_API int32_t nextera_n_labels(const struct nextera_context * ctx);
+NEXTERA_API const char * nextera_label(const struct nextera_context * ctx, int32_t i);
+NEXTERA_API int32_t nextera_token_cls(const struct nextera_context * ctx);
+NEXTERA_API int32_t nextera_token_sep(const struct nextera_context * ctx);
+NEXTERA_API int32_t nextera_token_pad(const struct nextera_context * ctx);
+NEXTERA_API int32_t nextera_token_mask(const struct nextera_context * ctx);
+NEXTERA_API const char * nextera_tokenizer_json(const struct nextera_context * ctx);
+NEXTERA_API const char * nextera_ftype(const struct nextera_context * ctx);
+/* keeps the reference's "linear layers: N int8 (...)" fragment (parsed by its python/bench.py) */
+NEXTERA_API const char * nextera_system_info(const struct nextera_context * ctx);
+
+/* host threads for load-time work (reference: src/nexterabert.h:68-69) */
+NEXTERA_API void    nextera_set_n_threads(struct nextera_context * ctx, int32_t n_threads);
+NEXTERA_API int32_t nextera_get_n_threads(const struct nextera_context * ctx);
+
+/* Encodes n_seqs unpadded sequences in one forward pass (reference:
+ * src/nexterabert.h:71-87).  tokens: sum(lengths) ids; hidden (optional):
+ * sum(lengths) x n_embd; pooled (optional): n_seqs x n_embd mean, L2-normalised
+ * when normalize != 0.  Host memory.  A sequence's result does not depend on
+ * the rest of the batch.  0 ok, 1 bad input, 2 allocation failure, 3 device failure. */
+NEXTERA_API int32_t nextera_encode(struct nextera_context * ctx,
+                                   const int32_t * tokens, const int32_t * lengths, int32_t n_seqs,
+                                   float * hidden, float * pooled, int32_t normalize);
+
+/* nextera_encode with optional segment ids (reference: src/nexterabert.h:95-98) */
+NEXTERA_API int32_t nextera_encode_segments(struct nextera_context * ctx,
+                                            const int32_t * tokens, const int32_t * token_types,
+                                            const int32_t * lengths, int32_t n_seqs,
+                                            float * hidden, float * pooled, int32_t normalize);
+
+/* Heads (reference: src/nexterabert.h:100-121).  Not on the GPU yet: these
+ * return 1 with a message on stderr. */
+NEXTERA_API int32_t nextera_pooler_output(struct nextera_context * ctx,
+                                          const int32_t * tokens, const int32_t * token_types,
+                                          const int32_t * lengths, int32_t n_seqs, float * out);
+NEXTERA_API int32_t nextera_classify(struct nextera_context * ctx,
+                                     const int32_t * tokens, const int32_t * token_types,
+                                     const int32_t * lengths, int32_t n_seqs, float * logits);
+NEXTERA_API int32_t nextera_mlm_logits(struct nextera_context * ctx,
+                                       const int32_t * tokens, int32_t n_tokens,
+                                       const int32_t * positions, int32_t n_pos,
+                                       float * logits);
+
+/* wall time of the last encode call in ms, host copies included (reference: src/nexterabert.h:124) */
+NEXTERA_API double nextera_last_ms(const struct nextera_context * ctx);
+
+/* ---- outside the reference's public header ---- */
+
+/* Exported by the reference without a header declaration (src/nexterabert.cpp:1818-1841);
+ * its CLI and Python binding bind them.  set_layers: run only the first n blocks and
+ * skip out_norm (-1: whole model).  profile: per-kind device time (int8 linear /
+ * attention / row ops) measured with CUDA events, printed by profile_print. */
+NEXTERA_API void nextera_debug_set_layers(struct nextera_context * ctx, int32_t n_layers);
+NEXTERA_API void nextera_debug_profile(struct nextera_context * ctx, int32_t enable);
+NEXTERA_API void nextera_debug_profile_print(const struct nextera_context * ctx);
+
+/* Device-resident variant of nextera_encode_segments: tokens / token_types are
+ * device pointers, hidden / pooled device pointers (either may be NULL), lengths
+ * host memory; work is enqueued on `stream` (cudaStream_t as void *) and this
+ * call returns once it is enqueued.  No counterpart in the reference (its data
+ * never leaves the host); used to time the forward with inputs already in HBM. */
+NEXTERA_API int32_t nextera_encode_device(struct nextera_context * ctx,
+                                          const int32_t * d_tokens, const int32_t * d_token_types,
+                                          const int32_t * lengths, int32_t n_seqs,
+                                          float * d_hidden, float * d_pooled, int32_t normalize,
+                                          void * stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NEXTERABERT_H */

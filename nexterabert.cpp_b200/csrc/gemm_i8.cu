@@ -1,0 +1,331 @@
+// int8 linear layer on the 5th-generation tensor cores (tcgen05, kind::i8).
+//
+//   out[t][n] = (res[t][n] +) sum_B fma(float(S_B[t][n]) * sx[t][B], sw[B][n], .)
+//   S_B       = sum over the 256 inputs of block B of xq[t][k] * w8[n][k]   (int32)
+//
+// which is the reference's op_linear_i8 (src/nexterabert.cpp:881-1007) with its
+// u8 activations written as s8 (u8 - 128): the reference's "off" term
+// -128 * sum(w8) cancels exactly, so the int32 block sums are identical, and
+// the fp32 epilogue performs the same operations in the same order (ascending
+// B from 0, residual added last), so outputs are bit-identical.
+//
+// Kernel shape (one CTA per SM, persistent over 128x128 output tiles, tile
+// index n-fastest so the CTAs in flight share their activation tiles in L2):
+//   warp 0      TMA producer: 128x128-byte tiles of xq and w8 (SWIZZLE_128B)
+//               into a 4-stage shared-memory ring
+//   warp 1      allocates TMEM (2 x 128 columns) and issues tcgen05.mma from one
+//               thread: 4 MMAs (K = 32 each) per 128-byte stage, one TMEM
+//               accumulator per 256-input block, alternating between the two
+//   warps 2-9   epilogue: tcgen05.ld the block's int32 sums (warp w reads TMEM
+//               lane quadrant w % 4, half the columns), release the buffer,
+//               fold the block into fp32 registers; after the last block add the
+//               residual and store
+// The per-block accumulator switch is what lets the int32 sums be scaled per
+// block: the MMA of block B+1 runs while the epilogue drains block B.
+#include "common.cuh"
+#include "ptx.cuh"
+#include "nextera_kernels.h"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+namespace nxk {
+
+extern __device__ int g_error;
+
+namespace gemm {
+
+constexpr int BM = 128, BN = 128, BKB = 128;      // tile rows, tile cols, K bytes per stage
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BKB, B_BYTES = BN * BKB, STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int EPI_WARPS = 8;
+constexpr int THREADS = 32 * (2 + EPI_WARPS);
+constexpr int TMEM_COLS = 2 * BN;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /* alignment */ + 256 /* barriers */;
+constexpr uint32_t IDESC = idesc_i8(BM, BN);
+
+enum : int { ERR_PRODUCER = 0x101, ERR_MMA = 0x102, ERR_EPILOGUE = 0x103 };
+
+struct Args {
+    const float * sx;
+    const float * sw;
+    const float * res;
+    float * out;
+    int T, N, K, n_blk, n_chunks, tiles_n, n_tiles;
+};
+
+__global__ void __launch_bounds__(THREADS, 1)
+gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, const Args a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
+    uint8_t * sA = smem;
+    uint8_t * sB = smem + STAGES * A_BYTES;
+    uint64_t * bars = (uint64_t *) (sB + STAGES * B_BYTES);
+    uint64_t * full = bars, * empty = bars + STAGES, * accf = bars + 2 * STAGES, * acce = bars + 2 * STAGES + 2;
+    uint32_t * tmem_slot = (uint32_t *) (bars + 2 * STAGES + 4);
+    volatile int * abort_flag = (volatile int *) (tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&empty[s]), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(smem_u32(&accf[b]), 1);
+            mbar_init(smem_u32(&acce[b]), EPI_WARPS);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&tm_a);
+        tma_prefetch_desc(&tm_b);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
+                const int m0 = (tile / a.tiles_n) * BM, n0 = (tile % a.tiles_n) * BN;
+                for (int c = 0; c < a.n_chunks; ++c, ++it) {
+                    const uint32_t s = it % STAGES, u = it / STAGES;
+                    if (u > 0 && !mbar_wait(smem_u32(&empty[s]), (u - 1) & 1)) { ok = false; break; }
+                    if (*abort_flag) { ok = false; break; }
+                    const uint32_t fb = smem_u32(&full[s]);
+                    mbar_arrive_expect_tx(fb, STAGE_BYTES);
+                    tma_load_2d(smem_u32(sA + s * A_BYTES), &tm_a, c * BKB, m0, fb);
+                    tma_load_2d(smem_u32(sB + s * B_BYTES), &tm_b, c * BKB, n0, fb);
+                }
+            }
+            if (!ok) {
+                *abort_flag = 1;
+                atomicExch(&g_error, ERR_PRODUCER);
+            }
+            // every issued copy lands before the CTA may exit
+            const uint32_t first = it > STAGES ? it - STAGES : 0;
+            for (uint32_t k = first; k < it; ++k) mbar_wait(smem_u32(&full[k % STAGES]), (k / STAGES) & 1);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            uint32_t it = 0, kb = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
+                for (int b = 0; ok && b < a.n_blk; ++b, ++kb) {
+                    const uint32_t acc = kb & 1, use = kb >> 1;
+                    if (use > 0 && !mbar_wait(smem_u32(&acce[acc]), (use - 1) & 1)) { ok = false; break; }
+                    if (*abort_flag) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t d = tmem + acc * BN;
+                    const int c0 = 2 * b, c1 = min(2 * b + 2, a.n_chunks);
+                    for (int c = c0; c < c1; ++c, ++it) {
+                        const uint32_t s = it % STAGES;
+                        if (!mbar_wait(smem_u32(&full[s]), (it / STAGES) & 1)) { ok = false; break; }
+                        tc_fence_after();
+                        const uint32_t abase = smem_u32(sA + s * A_BYTES), bbase = smem_u32(sB + s * B_BYTES);
+#pragma unroll
+                        for (int kk = 0; kk < BKB / 32; ++kk) {
+                            mma_i8(d, sdesc_k_sw128(abase + kk * 32), sdesc_k_sw128(bbase + kk * 32), IDESC,
+                                   (c > c0 || kk > 0) ? 1u : 0u);
+                        }
+                        mma_commit(smem_u32(&empty[s]));
+                    }
+                    if (!ok) break;
+                    mma_commit(smem_u32(&accf[acc]));
+                }
+            }
+            if (!ok) {
+                *abort_flag = 1;
+                atomicExch(&g_error, ERR_MMA);
+            }
+            // the last MMAs complete before TMEM is released
+            if (kb > 0) mbar_wait(smem_u32(&accf[(kb - 1) & 1]), ((kb - 1) >> 1) & 1);
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int quad = warp & 3, halfc = (warp - 2) >> 2;
+        const int row = 32 * quad + lane;
+        uint32_t kb = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
+            const int m0 = (tile / a.tiles_n) * BM, n0 = (tile % a.tiles_n) * BN;
+            const int t = m0 + row;
+            const int nc = n0 + 64 * halfc;
+            float f[64];
+#pragma unroll
+            for (int c = 0; c < 64; ++c) f[c] = 0.0f;
+            for (int b = 0; b < a.n_blk; ++b, ++kb) {
+                const uint32_t acc = kb & 1, use = kb >> 1;
+                const bool got = mbar_wait(smem_u32(&accf[acc]), use & 1) && !*abort_flag;
+                if (!__all_sync(0xffffffffu, got)) { ok = false; break; }   // warp-uniform
+                tc_fence_after();
+                uint32_t r0[32], r1[32];
+                const uint32_t taddr = tmem + ((uint32_t) (32 * quad) << 16) + acc * BN + 64 * halfc;
+                tmem_ld_32x32b_x32(taddr, r0);
+                tmem_ld_32x32b_x32(taddr + 32, r1);
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&acce[acc]));
+                if (nc >= a.N) continue;                                   // columns past N (N % 64 == 0)
+                const float sxb = t < a.T ? a.sx[(size_t) t * a.n_blk + b] : 0.0f;
+                const float * swp = a.sw + (size_t) b * a.N + nc;
+#pragma unroll
+                for (int c = 0; c < 32; ++c) {
+                    f[c] = __fmaf_rn(__fmul_rn(i2f_exact((int32_t) r0[c]), sxb), __ldg(swp + c), f[c]);
+                }
+#pragma unroll
+                for (int c = 0; c < 32; ++c) {
+                    f[32 + c] = __fmaf_rn(__fmul_rn(i2f_exact((int32_t) r1[c]), sxb), __ldg(swp + 32 + c), f[32 + c]);
+                }
+            }
+            if (!ok) break;
+            if (t < a.T && nc < a.N) {
+                float * o = a.out + (size_t) t * a.N + nc;
+                const float * rr = a.res ? a.res + (size_t) t * a.N + nc : nullptr;
+#pragma unroll
+                for (int c = 0; c < 64; c += 4) {
+                    float4 v = make_float4(f[c], f[c + 1], f[c + 2], f[c + 3]);
+                    if (rr) {
+                        const float4 r4 = *(const float4 *) (rr + c);
+                        v.x = __fadd_rn(r4.x, v.x); v.y = __fadd_rn(r4.y, v.y);
+                        v.z = __fadd_rn(r4.z, v.z); v.w = __fadd_rn(r4.w, v.w);
+                    }
+                    *(float4 *) (o + c) = v;
+                }
+            }
+        }
+        if (!ok) {
+            *abort_flag = 1;
+            atomicExch(&g_error, ERR_EPILOGUE);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// Validation kernel: same arithmetic on CUDA cores, one thread per output.
+__global__ void gemm_i8_simt(const int8_t * __restrict__ xq, const float * __restrict__ sx, int T,
+                             const int8_t * __restrict__ w8, const float * __restrict__ sw, int K, int N,
+                             const float * __restrict__ res, float * __restrict__ out, int32_t * __restrict__ sums) {
+    const size_t i = blockIdx.x * (size_t) blockDim.x + threadIdx.x;
+    if (i >= (size_t) T * N) return;
+    const int t = (int) (i / N), n = (int) (i % N);
+    const int n_blk = (K + I8_BLOCK - 1) / I8_BLOCK;
+    const int8_t * xr = xq + (size_t) t * K;
+    const int8_t * wr = w8 + (size_t) n * K;
+    float f = 0.0f;
+    for (int B = 0; B < n_blk; ++B) {
+        const int k0 = B * I8_BLOCK, k1 = min(K, k0 + I8_BLOCK);
+        int s = 0;
+        for (int k = k0; k < k1; k += 4) s = __dp4a(*(const int *) (xr + k), *(const int *) (wr + k), s);
+        if (sums) sums[((size_t) t * N + n) * n_blk + B] = s;
+        if (out) f = __fmaf_rn(__fmul_rn(i2f_exact(s), sx[(size_t) t * n_blk + B]), sw[(size_t) B * N + n], f);
+    }
+    if (out) out[i] = res ? __fadd_rn(res[i], f) : f;
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, []() {
+        void * p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) {
+            fn = (PFN_cuTensorMapEncodeTiled_v12000) p;
+        }
+    });
+    return fn;
+}
+
+// rows x K bytes, K-contiguous, boxes of 128 rows x 128 bytes in the 128-byte swizzle
+bool make_map(CUtensorMap * m, const void * base, uint64_t rows, uint64_t K) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = { (cuuint64_t) K, (cuuint64_t) rows };
+    cuuint64_t strides[1] = { (cuuint64_t) K };
+    cuuint32_t box[2] = { (cuuint32_t) BKB, (cuuint32_t) BM };
+    cuuint32_t estr[2] = { 1, 1 };
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int sm_count() {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+}
+
+} // namespace gemm
+} // namespace nxk
+
+using namespace nxk;
+
+extern "C" {
+
+int nxk_linear_i8(const int8_t * xq, const float * sx, int T, const int8_t * w8, const float * sw, int K, int N,
+                  const float * res, float * out, void * stream) {
+    using namespace nxk::gemm;
+    // TMA: K-byte row pitch a multiple of 16, 16-byte aligned bases; each epilogue
+    // warp owns 64 output columns, so N must be a multiple of 64
+    if (T < 0 || K <= 0 || N <= 0 || (K & 31) || (N & 63) || !xq || !w8 || !sx || !sw || !out) return NXK_EINVAL;
+    if (((uintptr_t) xq & 15) || ((uintptr_t) w8 & 15) || ((uintptr_t) out & 15)) return NXK_EINVAL;
+    if (res && ((uintptr_t) res & 15)) return NXK_EINVAL;
+    if (T == 0) return NXK_OK;
+    CUtensorMap ma, mb;
+    if (!make_map(&ma, xq, (uint64_t) T, (uint64_t) K) || !make_map(&mb, w8, (uint64_t) N, (uint64_t) K)) return NXK_ELAUNCH;
+    static std::once_flag attr_once;
+    std::call_once(attr_once, []() {
+        cudaFuncSetAttribute(gemm_i8_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    });
+    Args a;
+    a.sx = sx; a.sw = sw; a.res = res; a.out = out;
+    a.T = T; a.N = N; a.K = K;
+    a.n_blk = (K + I8_BLOCK - 1) / I8_BLOCK;
+    a.n_chunks = (K + BKB - 1) / BKB;
+    a.tiles_n = (N + BN - 1) / BN;
+    a.n_tiles = ((T + BM - 1) / BM) * a.tiles_n;
+    const int grid = min(a.n_tiles, sm_count());
+    gemm_i8_tc<<<grid, THREADS, SMEM_BYTES, (cudaStream_t) stream>>>(ma, mb, a);
+    return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
+}
+
+int nxk_linear_i8_simt(const int8_t * xq, const float * sx, int T, const int8_t * w8, const float * sw, int K, int N,
+                       const float * res, float * out, void * stream) {
+    if (T < 0 || K <= 0 || N <= 0 || (K & 3)) return NXK_EINVAL;
+    const size_t n = (size_t) T * N;
+    if (!n) return NXK_OK;
+    nxk::gemm::gemm_i8_simt<<<(unsigned) ((n + 255) / 256), 256, 0, (cudaStream_t) stream>>>(
+        xq, sx, T, w8, sw, K, N, res, out, nullptr);
+    return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
+}
+
+int nxk_block_sums(const int8_t * xq, int T, const int8_t * w8, int K, int N, int32_t * sums, void * stream) {
+    if (T < 0 || K <= 0 || N <= 0 || (K & 3)) return NXK_EINVAL;
+    const size_t n = (size_t) T * N;
+    if (!n) return NXK_OK;
+    nxk::gemm::gemm_i8_simt<<<(unsigned) ((n + 255) / 256), 256, 0, (cudaStream_t) stream>>>(
+        xq, nullptr, T, w8, nullptr, K, N, nullptr, nullptr, sums);
+    return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
+}
+
+} // extern "C"

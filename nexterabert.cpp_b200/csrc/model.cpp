@@ -1,0 +1,1015 @@
+// libnexterabert.so host side: the nexterabert.h C API on one CUDA device.
+//
+// Mirrors the reference runtime's structure (src/nexterabert.cpp) with the
+// compute moved to sm_100a kernels (nextera_kernels.h):
+//   nextera_load     GGUF parse, hparams / block types / required-tensor checks
+//                    with the reference's messages (:1549-1775); quantized
+//                    linear weights are uploaded in their file blocks and
+//                    expanded to int8 + per-block scales on the device
+//                    (build_i8_weight, :1010-1049); conv kernels go tap-major
+//   nextera_encode   prepare_batch (:1341-1370), then the encoder of
+//                    builder::encoder (:1271-1294) as a sequence of kernel
+//                    launches on the context's stream, then pooling (:1903-1918)
+// Activation buffers live in a grow-only device arena sized for the largest
+// batch seen; a call runs with no device allocation once the arena is large
+// enough.  Every row op that feeds only int8 linears writes int8 codes
+// directly (the reference's int8_only, :1080-1085).
+#include "nexterabert.h"
+#include "nextera_kernels.h"
+#include "gguf.hpp"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <thread>
+#include <unordered_map>
+#include <vector>
+
+namespace {
+
+enum mixer_type { MIX_LILY, MIX_SWA, MIX_ATTN, MIX_HRA };
+enum ssmax_mode { SSMAX_SSSMAX, SSMAX_SSMAX, SSMAX_NONE };
+enum cls_task { CLS_NONE, CLS_SEQUENCE, CLS_CHOICE, CLS_TOKEN, CLS_QA };
+const char * const CLS_NAMES[] = { "", "sequence-classification", "multiple-choice", "token-classification",
+                                   "question-answering" };
+constexpr int I8_BLOCK = 256;
+
+struct hparams {
+    int32_t n_vocab = 0, n_embd = 0, n_layer = 0, n_inter = 0, n_head = 0, n_kv_head = 0, head_dim = 0;
+    int32_t lily_rank = 0, lily_kernel = 0, hra_block = 0, swa_window = 0, ntk_train_len = 0;
+    float rope_base = 100000.0f, swa_rope_base = 10000.0f, ssmax_base = 0.1f, rms_eps = 1e-8f, ln_eps = 1e-5f;
+    ssmax_mode ssmax = SSMAX_SSSMAX;
+    std::vector<mixer_type> block_types;
+    int32_t cls_id = -1, sep_id = -1, pad_id = -1, mask_id = -1;
+    bool has_mlm = false, has_pooler = false;
+    int32_t n_types = 0;
+    cls_task cls = CLS_NONE;
+    int32_t n_labels = 0;
+    std::vector<std::string> labels;
+};
+
+struct DevBuf {
+    void * p = nullptr;
+    size_t bytes = 0;
+    ~DevBuf() { if (p) cudaFree(p); }
+    bool alloc(size_t n) {
+        if (p) { cudaFree(p); p = nullptr; bytes = 0; }
+        if (!n) return true;
+        if (cudaMalloc(&p, n) != cudaSuccess) { p = nullptr; cudaGetLastError(); return false; }
+        bytes = n;
+        return true;
+    }
+    bool reserve(size_t n) { return n <= bytes ? true : alloc(n); }
+    template <class T> T * as() const { return (T *) p; }
+};
+
+struct I8Weight {
+    int n_in = 0, n_out = 0;
+    DevBuf w, scale;
+};
+
+struct RawTensor {          // a tensor kept in its file layout on the device
+    int type = 0;
+    int64_t ne[4] = {1, 1, 1, 1};
+    DevBuf d;
+};
+
+struct ConvTaps {
+    int k = 0, C = 0;
+    DevBuf taps;             // [k][C] tap-major
+};
+
+// device time per kind of kernel, as the reference's profiler reports per kind of custom op
+enum prof_kind { PROF_LINEAR, PROF_ATTN, PROF_ROWS, PROF_COUNT };
+const char * const PROF_NAMES[PROF_COUNT] = { "int8 linear", "attention", "norm / conv / gate / quantize" };
+
+struct profiler {
+    bool enabled = false;
+    double ms[PROF_COUNT] = {};
+    double total_ms = 0.0;
+    int64_t calls = 0;
+    std::vector<std::pair<cudaEvent_t, int>> marks;   // event recorded before each launch group
+};
+
+} // namespace
+
+struct nextera_context {
+    hparams hp;
+    std::string tokenizer_json, ftype, sysinfo, path;
+    int device = 0;
+    int n_threads = 1;
+    cudaStream_t stream = nullptr;
+
+    std::unordered_map<std::string, I8Weight> i8;
+    std::unordered_map<std::string, DevBuf> f32;          // 1-D fp32 parameters on the device
+    std::unordered_map<std::string, std::vector<float>> host_f32;   // the same, on the host (SSMax scalars)
+    std::unordered_map<std::string, ConvTaps> taps;
+    std::unordered_map<std::string, RawTensor> raw;       // embedding tables
+    std::vector<std::string> names;                       // every tensor in the file
+
+    // forward arena
+    DevBuf X, X2, U, Fa, Fb, Fc, Q1, Q1s, Q2, Q2s;
+    DevBuf meta, attn_ws, pooled;
+    int64_t cap_T = 0, cap_docs = 0;
+    // host staging (pinned)
+    void * h_stage = nullptr;
+    size_t h_stage_bytes = 0;
+    // rope tables on the device: [0] attn / hra base (NTK-stretched when needed), [1] swa
+    DevBuf rope_cos[2], rope_sin[2];
+    int rope_n[2] = {0, 0};
+    float rope_base_cached[2] = {0.0f, 0.0f};
+
+    int32_t debug_n_layers = -1;
+    profiler prof;
+    double last_ms = 0.0;
+
+    bool has(const std::string & n) const {
+        return i8.count(n) || f32.count(n) || taps.count(n) || raw.count(n) ||
+               std::find(names.begin(), names.end(), n) != names.end();
+    }
+};
+
+namespace {
+
+const char * ftype_name(uint32_t ft) {
+    switch (ft) {
+        case 0: return "F32"; case 1: return "F16"; case 2: return "Q4_0"; case 3: return "Q4_1";
+        case 7: return "Q8_0"; case 8: return "Q5_0"; case 9: return "Q5_1"; case 10: return "Q2_K";
+        case 11: return "Q3_K_S"; case 12: return "Q3_K_M"; case 13: return "Q3_K_L"; case 14: return "Q4_K_S";
+        case 15: return "Q4_K_M"; case 16: return "Q5_K_S"; case 17: return "Q5_K_M"; case 18: return "Q6_K";
+        default: return "unknown";
+    }
+}
+
+bool ends_with(const std::string & s, const char * suf) {
+    const size_t n = strlen(suf);
+    return s.size() >= n && s.compare(s.size() - n, n, suf) == 0;
+}
+
+// Every tensor the encoder and the file's heads need (the reference's required_tensors, :1483-1516)
+std::vector<std::string> required_tensors(const hparams & hp) {
+    std::vector<std::string> r = { "embedding.weight", "out_norm.weight", "out_norm.bias" };
+    auto add = [&r](const std::string & pre, std::initializer_list<const char *> names) {
+        for (const char * n : names) r.push_back(pre + n);
+    };
+    for (int l = 0; l < hp.n_layer && l < (int) hp.block_types.size(); ++l) {
+        const std::string blk = "blocks." + std::to_string(l) + ".", pre = blk + "attn.";
+        add(blk, { "attn_norm.weight", "mlp_norm.weight", "mlp.c_fc.weight", "mlp.c_proj.weight" });
+        add(pre, { "c_proj.weight" });
+        const mixer_type mt = hp.block_types[l];
+        if (mt == MIX_LILY) {
+            add(pre, { "ltc_conv.in_proj.weight", "ltc_conv.A.weight", "ltc_conv.kernel", "ltc_conv.out_proj.weight",
+                       "x_proj.weight", "B_proj.weight", "state_conv.depthwise.weight" });
+            continue;
+        }
+        add(pre, { "c_q.weight", "c_k.weight", "c_v.weight", "c_gate.weight",
+                   "q_norm.alpha", "q_norm.beta", "k_norm.alpha", "k_norm.beta" });
+        if (mt == MIX_HRA) {
+            add(pre, { "qkv_in.weight", "qkv_gate.weight", "c_C.weight",
+                       "qkv_conv.depthwise.weight", "c_o.depthwise.weight" });
+        }
+        if (mt != MIX_SWA && hp.ssmax != SSMAX_NONE) {
+            add(pre, { "scalable_factor.s" });
+            if (hp.ssmax == SSMAX_SSSMAX) add(pre, { "scalable_factor.b" });
+        }
+    }
+    if (hp.has_mlm) add("mlm.", { "dense.weight", "norm.weight", "bias" });
+    if (hp.cls != CLS_NONE) {
+        add("classifier.", { "weight", "bias" });
+        const bool pooled = hp.cls == CLS_SEQUENCE || hp.cls == CLS_CHOICE;
+        add(pooled ? "pooler." : "head.", { "dense.weight", "norm.weight" });
+    }
+    return r;
+}
+
+// fp32 cos / sin tables exactly as the reference builds them (build_rope, :1322-1338)
+void rope_table(int n_pos, float base, int head_dim, std::vector<float> & c, std::vector<float> & s) {
+    const int half = head_dim / 2;
+    c.resize((size_t) n_pos * half);
+    s.resize((size_t) n_pos * half);
+    std::vector<float> inv(half);
+    for (int i = 0; i < half; ++i) inv[i] = 1.0f / std::pow(base, (float) (2 * i) / (float) head_dim);
+    for (int t = 0; t < n_pos; ++t) {
+        for (int i = 0; i < half; ++i) {
+            const float a = (float) t * inv[i];
+            c[(size_t) t * half + i] = std::cos(a);
+            s[(size_t) t * half + i] = std::sin(a);
+        }
+    }
+}
+
+bool check(int rc, const char * what) {
+    if (rc != NXK_OK) {
+        fprintf(stderr, "nexterabert: kernel '%s' rejected its arguments or failed to launch (%d)\n", what, rc);
+        return false;
+    }
+    return true;
+}
+
+size_t align_up(size_t n, size_t a) { return (n + a - 1) / a * a; }
+
+} // namespace
+
+// ---------------------------------------------------------------------------
+// C API
+// ---------------------------------------------------------------------------
+
+struct nextera_params nextera_default_params(void) {
+    nextera_params p;
+    p.n_threads = 0;
+    p.use_repack = 1;
+    p.use_int8 = 1;
+    p.verbosity = 0;
+    return p;
+}
+
+struct nextera_context * nextera_load(const char * path, struct nextera_params params) {
+    const auto t_start = std::chrono::steady_clock::now();
+    nxg::File gg;
+    if (!gg.open(path)) {
+        fprintf(stderr, "nexterabert: failed to open '%s' (%s)\n", path, gg.error.c_str());
+        return nullptr;
+    }
+    if (gg.str("general.architecture", "") != "nexterabert") {
+        fprintf(stderr, "nexterabert: '%s' is not a nexterabert GGUF (general.architecture = '%s')\n", path,
+                gg.str("general.architecture", "").c_str());
+        return nullptr;
+    }
+    int n_dev = 0;
+    if (cudaGetDeviceCount(&n_dev) != cudaSuccess || n_dev == 0) {
+        cudaGetLastError();
+        fprintf(stderr, "nexterabert: no CUDA device\n");
+        return nullptr;
+    }
+    std::unique_ptr<nextera_context> c(new nextera_context());
+    c->path = path;
+    cudaGetDevice(&c->device);
+    hparams & hp = c->hp;
+    bool ok = true;
+    auto req_u32 = [&](const char * key) -> int32_t {
+        const nxg::Value * v = gg.get(key);
+        if (!v) { fprintf(stderr, "nexterabert: missing key '%s'\n", key); ok = false; return 0; }
+        return (int32_t) v->u;
+    };
+    hp.n_vocab = req_u32("nexterabert.vocab_size");
+    hp.n_embd = req_u32("nexterabert.embedding_length");
+    hp.n_layer = req_u32("nexterabert.block_count");
+    hp.n_inter = req_u32("nexterabert.feed_forward_length");
+    hp.n_head = req_u32("nexterabert.attention.head_count");
+    hp.n_kv_head = req_u32("nexterabert.attention.head_count_kv");
+    if (!ok) return nullptr;
+    hp.head_dim = hp.n_head > 0 ? hp.n_embd / hp.n_head : 0;
+    hp.lily_rank = (int32_t) gg.u32("nexterabert.lily.low_rank", (uint32_t) hp.head_dim);
+    hp.lily_kernel = (int32_t) gg.u32("nexterabert.lily.kernel_size", 5);
+    hp.hra_block = (int32_t) gg.u32("nexterabert.hra.block_size", 4);
+    hp.swa_window = (int32_t) gg.u32("nexterabert.swa.window", 256);
+    hp.ntk_train_len = (int32_t) gg.u32("nexterabert.rope.ntk_train_length", 0);
+    hp.rope_base = gg.f32("nexterabert.rope.freq_base", 100000.0f);
+    hp.swa_rope_base = gg.f32("nexterabert.swa.rope.freq_base", 10000.0f);
+    hp.ssmax_base = gg.f32("nexterabert.ssmax.base", 0.1f);
+    hp.rms_eps = gg.f32("nexterabert.rms_norm_epsilon", 1e-8f);
+    hp.ln_eps = gg.f32("nexterabert.layer_norm_epsilon", 1e-5f);
+    hp.cls_id = (int32_t) gg.u32("tokenizer.ggml.cls_token_id", (uint32_t) -1);
+    hp.sep_id = (int32_t) gg.u32("tokenizer.ggml.seperator_token_id", (uint32_t) -1);
+    hp.pad_id = (int32_t) gg.u32("tokenizer.ggml.padding_token_id", (uint32_t) -1);
+    hp.mask_id = (int32_t) gg.u32("tokenizer.ggml.mask_token_id", (uint32_t) -1);
+    if (const nxg::Value * v = gg.get("nexterabert.mlm_head")) hp.has_mlm = v->u != 0;
+    const std::string task = gg.str("nexterabert.classifier.task", "");
+    for (int i = CLS_SEQUENCE; i <= CLS_QA; ++i) {
+        if (task == CLS_NAMES[i]) hp.cls = (cls_task) i;
+    }
+    if (const nxg::Value * v = gg.get("nexterabert.classifier.labels")) hp.labels = v->arr_s;
+    const std::string mode = gg.str("nexterabert.ssmax.mode", "sssmax");
+    hp.ssmax = mode == "none" ? SSMAX_NONE : mode == "ssmax" ? SSMAX_SSMAX : SSMAX_SSSMAX;
+    if (!task.empty() && hp.cls == CLS_NONE) {
+        fprintf(stderr, "nexterabert: unsupported classifier task '%s'\n", task.c_str());
+        ok = false;
+    }
+    {
+        const nxg::Value * v = gg.get("nexterabert.block_types");
+        const size_t n = v ? v->arr_s.size() : 0;
+        if ((int32_t) n != hp.n_layer) {
+            fprintf(stderr, "nexterabert: block_types has %zu entries, expected %d\n", n, hp.n_layer);
+            ok = false;
+        }
+        for (size_t i = 0; ok && i < n; ++i) {
+            const std::string & t = v->arr_s[i];
+            if (t == "lily") hp.block_types.push_back(MIX_LILY);
+            else if (t == "swa") hp.block_types.push_back(MIX_SWA);
+            else if (t == "attn") hp.block_types.push_back(MIX_ATTN);
+            else if (t == "hra") hp.block_types.push_back(MIX_HRA);
+            else { fprintf(stderr, "nexterabert: unsupported block type '%s'\n", t.c_str()); ok = false; }
+        }
+    }
+    if (hp.head_dim % 2 != 0 || hp.n_kv_head <= 0 || hp.n_head % hp.n_kv_head != 0) {
+        fprintf(stderr, "nexterabert: unsupported head layout\n");
+        ok = false;
+    }
+    // limits of the device kernels
+    if (ok && (hp.head_dim != 64 || hp.n_embd % 64 || hp.n_inter % 64 || (hp.n_head / hp.n_kv_head) > 4)) {
+        fprintf(stderr, "nexterabert: this build runs head_dim 64, n_embd / n_inter multiples of 64 and at most "
+                        "4 query heads per KV head (file: head_dim %d, n_embd %d, n_inter %d, %d:%d heads)\n",
+                hp.head_dim, hp.n_embd, hp.n_inter, hp.n_head, hp.n_kv_head);
+        ok = false;
+    }
+    c->tokenizer_json = gg.str("tokenizer.huggingface.json", "");
+    c->ftype = ftype_name(gg.u32("general.file_type", 0));
+    if (!ok) return nullptr;
+
+    int hw = (int) std::max(1u, std::thread::hardware_concurrency());
+    c->n_threads = params.n_threads > 0 ? params.n_threads : hw;
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        fprintf(stderr, "nexterabert: cannot create a CUDA stream\n");
+        return nullptr;
+    }
+
+    FILE * f = fopen(path, "rb");
+    if (!f) {
+        fprintf(stderr, "nexterabert: failed to open '%s'\n", path);
+        return nullptr;
+    }
+    std::vector<uint8_t> tmp;
+    DevBuf staging;
+    size_t weight_bytes = 0;
+    for (const nxg::TensorInfo & t : gg.tensors) {
+        c->names.push_back(t.name);
+        const size_t n = t.nbytes;
+        tmp.resize(n ? n : 1);
+        if (fseeko(f, (off_t) (gg.data_offset + t.offset), SEEK_SET) != 0 || fread(tmp.data(), 1, n, f) != n) {
+            fprintf(stderr, "nexterabert: failed to read tensor '%s'\n", t.name.c_str());
+            ok = false;
+            break;
+        }
+        const int n_dims = t.ne[3] > 1 ? 4 : t.ne[2] > 1 ? 3 : t.ne[1] > 1 ? 2 : 1;
+        const bool embedding = t.name == "embedding.weight" || t.name == "mlm.decoder.weight" ||
+                               t.name == "token_type_embeddings.weight";
+        const bool gemm = !embedding && n_dims == 2 && nxg::is_quantized(t.type);
+        if (gemm && t.ne[0] % 32 == 0 && t.ne[1] % 4 == 0) {
+            // int8 path (:1663-1667): blocks to the device, expanded there
+            I8Weight & w = c->i8[t.name];
+            w.n_in = (int) t.ne[0];
+            w.n_out = (int) t.ne[1];
+            const int n_blk = (w.n_in + I8_BLOCK - 1) / I8_BLOCK;
+            if (!staging.reserve(n) || !w.w.alloc((size_t) w.n_in * w.n_out) ||
+                !w.scale.alloc(sizeof(float) * (size_t) n_blk * w.n_out)) {
+                fprintf(stderr, "nexterabert: out of device memory loading '%s'\n", t.name.c_str());
+                ok = false;
+                break;
+            }
+            cudaMemcpyAsync(staging.p, tmp.data(), n, cudaMemcpyHostToDevice, c->stream);
+            if (!check(nxk_expand_weight(t.type, staging.p, w.n_in, w.n_out, w.w.as<int8_t>(), w.scale.as<float>(),
+                                         nullptr, c->stream), "expand_weight")) {
+                ok = false;
+                break;
+            }
+            cudaStreamSynchronize(c->stream);   // staging is reused by the next tensor
+            weight_bytes += (size_t) w.n_in * w.n_out + sizeof(float) * (size_t) n_blk * w.n_out;
+            continue;
+        }
+        if (embedding) {
+            RawTensor & r = c->raw[t.name];
+            r.type = t.type;
+            memcpy(r.ne, t.ne, sizeof(r.ne));
+            if (!r.d.alloc(n)) { ok = false; break; }
+            cudaMemcpy(r.d.p, tmp.data(), n, cudaMemcpyHostToDevice);
+            weight_bytes += n;
+            continue;
+        }
+        if (ends_with(t.name, ".depthwise.weight") || ends_with(t.name, ".kernel")) {
+            // conv kernels are stored (k, C) per channel; the kernels want one row per tap (:1702-1711)
+            if (t.type != 0) {
+                fprintf(stderr, "nexterabert: conv kernel '%s' must be F32\n", t.name.c_str());
+                ok = false;
+                break;
+            }
+            ConvTaps & ct = c->taps[t.name];
+            ct.k = (int) t.ne[0];
+            ct.C = (int) t.ne[1];
+            std::vector<float> tm((size_t) ct.k * ct.C);
+            const float * src = (const float *) tmp.data();
+            for (int ch = 0; ch < ct.C; ++ch) {
+                for (int j = 0; j < ct.k; ++j) tm[(size_t) j * ct.C + ch] = src[(size_t) ch * ct.k + j];
+            }
+            if (!ct.taps.alloc(tm.size() * sizeof(float))) { ok = false; break; }
+            cudaMemcpy(ct.taps.p, tm.data(), tm.size() * sizeof(float), cudaMemcpyHostToDevice);
+            continue;
+        }
+        if (n_dims == 1 && t.type == 0) {
+            std::vector<float> & hv = c->host_f32[t.name];
+            hv.assign((const float *) tmp.data(), (const float *) tmp.data() + t.ne[0]);
+            DevBuf & d = c->f32[t.name];
+            if (!d.alloc(n)) { ok = false; break; }
+            cudaMemcpy(d.p, tmp.data(), n, cudaMemcpyHostToDevice);
+            continue;
+        }
+        if (gemm || n_dims == 2) {
+            // F32 / F16 matrices would run on ggml's mul_mat in the reference (:1140-1142)
+            const bool needed_by_encoder = t.name.rfind("blocks.", 0) == 0;
+            if (needed_by_encoder) {
+                fprintf(stderr, "nexterabert: '%s' (type %d) is not a quantized matrix this build can expand to "
+                                "int8; float and unaligned GEMM weights are not supported on the GPU path\n",
+                        t.name.c_str(), t.type);
+                ok = false;
+                break;
+            }
+        }
+    }
+    fclose(f);
+    if (ok && cudaStreamSynchronize(c->stream) != cudaSuccess) {
+        fprintf(stderr, "nexterabert: device error while expanding weights: %s\n", cudaGetErrorString(cudaGetLastError()));
+        ok = false;
+    }
+    if (!ok) return nullptr;
+
+    hp.has_pooler = c->has("pooler.dense.weight") && c->has("pooler.norm.weight");
+    if (c->raw.count("token_type_embeddings.weight")) hp.n_types = (int32_t) c->raw["token_type_embeddings.weight"].ne[1];
+    if (hp.cls != CLS_NONE && c->host_f32.count("classifier.bias")) {
+        hp.n_labels = (int32_t) c->host_f32["classifier.bias"].size();
+        if ((int32_t) hp.labels.size() != hp.n_labels) hp.labels.clear();
+    }
+    for (const std::string & name : required_tensors(hp)) {
+        if (c->has(name)) continue;
+        fprintf(stderr, "nexterabert: '%s' has no tensor '%s': not a complete nexterabert file "
+                        "(convert the checkpoint again with python/convert_hf_to_gguf.py)\n", path, name.c_str());
+        return nullptr;
+    }
+    // every encoder linear must be on the int8 path
+    for (int l = 0; l < hp.n_layer; ++l) {
+        const std::string blk = "blocks." + std::to_string(l) + ".";
+        for (const std::string & n : required_tensors(hp)) {
+            if (n.rfind(blk, 0) == 0 && ends_with(n, ".weight") && !c->taps.count(n) && !c->f32.count(n) &&
+                !c->i8.count(n)) {
+                fprintf(stderr, "nexterabert: '%s' is not on the int8 path\n", n.c_str());
+                return nullptr;
+            }
+        }
+    }
+
+    cudaDeviceProp prop;
+    cudaGetDeviceProperties(&prop, c->device);
+    char info[512];
+    snprintf(info, sizeof(info),
+             "CUDA = 1 | device = %s (sm_%d%d, %d SMs) | linear layers: %d int8 (tcgen05 kind::i8), 0 ggml repack | "
+             "custom ops: CUDA sm_100a",
+             prop.name, prop.major, prop.minor, prop.multiProcessorCount, (int) c->i8.size());
+    c->sysinfo = info;
+    if (params.verbosity > 0) {
+        const double ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t_start).count();
+        fprintf(stderr, "nexterabert: %s | %s | %d layers, n_embd %d | device weights %.1f MiB | loaded in %.0f ms\n",
+                path, c->ftype.c_str(), hp.n_layer, hp.n_embd, weight_bytes / 1048576.0, ms);
+        fprintf(stderr, "nexterabert: %s\n", c->sysinfo.c_str());
+    }
+    return c.release();
+}
+
+void nextera_free(struct nextera_context * c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    for (auto & m : c->prof.marks) cudaEventDestroy(m.first);
+    if (c->h_stage) cudaFreeHost(c->h_stage);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+int32_t nextera_n_embd(const struct nextera_context * c) { return c->hp.n_embd; }
+int32_t nextera_n_vocab(const struct nextera_context * c) { return c->hp.n_vocab; }
+int32_t nextera_n_layer(const struct nextera_context * c) { return c->hp.n_layer; }
+int32_t nextera_has_mlm_head(const struct nextera_context * c) { return c->hp.has_mlm ? 1 : 0; }
+int32_t nextera_has_pooler(const struct nextera_context * c) { return c->hp.has_pooler ? 1 : 0; }
+int32_t nextera_n_token_types(const struct nextera_context * c) { return c->hp.n_types; }
+int32_t nextera_n_labels(const struct nextera_context * c) { return c->hp.n_labels; }
+const char * nextera_classifier_task(const struct nextera_context * c) { return CLS_NAMES[c->hp.cls]; }
+const char * nextera_label(const struct nextera_context * c, int32_t i) {
+    return i >= 0 && i < (int32_t) c->hp.labels.size() ? c->hp.labels[i].c_str() : "";
+}
+int32_t nextera_token_cls(const struct nextera_context * c) { return c->hp.cls_id; }
+int32_t nextera_token_sep(const struct nextera_context * c) { return c->hp.sep_id; }
+int32_t nextera_token_pad(const struct nextera_context * c) { return c->hp.pad_id; }
+int32_t nextera_token_mask(const struct nextera_context * c) { return c->hp.mask_id; }
+const char * nextera_tokenizer_json(const struct nextera_context * c) { return c->tokenizer_json.c_str(); }
+const char * nextera_ftype(const struct nextera_context * c) { return c->ftype.c_str(); }
+const char * nextera_system_info(const struct nextera_context * c) { return c->sysinfo.c_str(); }
+int32_t nextera_get_n_threads(const struct nextera_context * c) { return c->n_threads; }
+double nextera_last_ms(const struct nextera_context * c) { return c->last_ms; }
+void nextera_set_n_threads(struct nextera_context * c, int32_t n) {
+    c->n_threads = n > 0 ? n : (int) std::max(1u, std::thread::hardware_concurrency());
+}
+
+void nextera_debug_set_layers(struct nextera_context * c, int32_t n_layers) { c->debug_n_layers = n_layers; }
+
+void nextera_debug_profile(struct nextera_context * c, int32_t enable) {
+    for (auto & m : c->prof.marks) cudaEventDestroy(m.first);
+    c->prof = profiler();
+    c->prof.enabled = enable != 0;
+}
+
+void nextera_debug_profile_print(const struct nextera_context * c) {
+    const profiler & pr = c->prof;
+    if (!pr.calls) return;
+    double sum = 0.0;
+    fprintf(stderr, "profile over %lld forward passes (ms per pass, device time):\n", (long long) pr.calls);
+    for (int i = 0; i < PROF_COUNT; ++i) {
+        sum += pr.ms[i];
+        fprintf(stderr, "  %-22s %8.3f  %5.1f%%\n", PROF_NAMES[i], pr.ms[i] / pr.calls,
+                pr.total_ms > 0 ? 100.0 * pr.ms[i] / pr.total_ms : 0.0);
+    }
+    fprintf(stderr, "  %-22s %8.3f  %5.1f%%   (host work, copies, launch gaps)\n", "everything else",
+            (pr.total_ms - sum) / pr.calls, pr.total_ms > 0 ? 100.0 * (pr.total_ms - sum) / pr.total_ms : 0.0);
+    fprintf(stderr, "  %-22s %8.3f\n", "total", pr.total_ms / pr.calls);
+}
+
+// ---------------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------------
+namespace {
+
+struct Batch {
+    int n_docs = 0, T = 0, nb = 0, max_len = 0;
+    std::vector<int32_t> start, len, bstart, blen, row_doc, brow_doc;
+};
+
+// device views of one forward's layout
+struct Layout {
+    const int32_t * row_doc, * start, * len, * bstart, * blen, * brow_doc, * tokens, * types;
+};
+
+class Forward {
+public:
+    Forward(nextera_context & c, cudaStream_t s) : c_(c), s_(s), hp_(c.hp) {}
+
+    bool ok = true;
+
+    void mark(int kind) {
+        if (!c_.prof.enabled) return;
+        cudaEvent_t e;
+        cudaEventCreate(&e);
+        cudaEventRecord(e, s_);
+        c_.prof.marks.emplace_back(e, kind);
+    }
+
+    // y = W x (+ res): x = (q, sx) with T rows
+    void linear(const std::string & name, const int8_t * q, const float * sx, int T, const float * res, float * out) {
+        if (!ok) return;
+        auto it = c_.i8.find(name);
+        if (it == c_.i8.end()) {
+            fprintf(stderr, "nexterabert: missing tensor '%s'\n", name.c_str());
+            ok = false;
+            return;
+        }
+        mark(PROF_LINEAR);
+        const I8Weight & w = it->second;
+        ok = check(nxk_linear_i8(q, sx, T, w.w.as<int8_t>(), w.scale.as<float>(), w.n_in, w.n_out, res, out, s_),
+                   name.c_str());
+    }
+
+    int n_out(const std::string & name) const {
+        auto it = c_.i8.find(name);
+        return it == c_.i8.end() ? 0 : it->second.n_out;
+    }
+
+    const float * p(const std::string & name) {
+        auto it = c_.f32.find(name);
+        if (it == c_.f32.end()) {
+            fprintf(stderr, "nexterabert: missing tensor '%s'\n", name.c_str());
+            ok = false;
+            return nullptr;
+        }
+        return it->second.as<float>();
+    }
+
+    const ConvTaps * taps(const std::string & name) {
+        auto it = c_.taps.find(name);
+        if (it == c_.taps.end()) {
+            fprintf(stderr, "nexterabert: missing tensor '%s'\n", name.c_str());
+            ok = false;
+            return nullptr;
+        }
+        return &it->second;
+    }
+
+    void rows(int rc, const char * what) {
+        if (ok) ok = check(rc, what);
+    }
+
+    // Scalable-Softmax scale for n attended keys (ssmax_scale, :1174-1181)
+    float ssmax_scale(const std::string & pre, int n) const {
+        if (hp_.ssmax == SSMAX_NONE) return 1.0f;
+        const float s = c_.host_f32.at(pre + "scalable_factor.s")[0];
+        const float ln = std::log((float) std::max(n, 1));
+        if (hp_.ssmax == SSMAX_SSMAX) return s * ln;
+        const float b = c_.host_f32.at(pre + "scalable_factor.b")[0];
+        return s * ln + hp_.ssmax_base + std::max(b, 0.0f);
+    }
+
+    nextera_context & c_;
+    cudaStream_t s_;
+    const hparams & hp_;
+};
+
+// Lays out the batch and checks it (prepare_batch :1341-1370, check_tokens / check_types :1843-1863)
+int prepare(const nextera_context & c, const int32_t * tokens, const int32_t * types, const int32_t * lengths,
+            int32_t n_seqs, bool tokens_on_host, Batch & b, float & rope0_base) {
+    if (n_seqs <= 0 || !lengths) return 1;
+    b.n_docs = n_seqs;
+    b.start.resize(n_seqs);
+    b.len.assign(lengths, lengths + n_seqs);
+    b.bstart.resize(n_seqs);
+    b.blen.resize(n_seqs);
+    int64_t total = 0, btotal = 0;
+    for (int i = 0; i < n_seqs; ++i) {
+        if (lengths[i] <= 0) {
+            fprintf(stderr, "nexterabert: empty sequence in batch\n");
+            return 1;
+        }
+        b.start[i] = (int32_t) total;
+        total += lengths[i];
+        b.blen[i] = (lengths[i] + c.hp.hra_block - 1) / c.hp.hra_block;
+        b.bstart[i] = (int32_t) btotal;
+        btotal += b.blen[i];
+        b.max_len = std::max(b.max_len, lengths[i]);
+    }
+    if (total > INT32_MAX / 4) {
+        fprintf(stderr, "nexterabert: batch too large\n");
+        return 1;
+    }
+    b.T = (int) total;
+    b.nb = (int) btotal;
+    b.row_doc.resize(b.T);
+    b.brow_doc.resize(b.nb);
+    for (int i = 0; i < n_seqs; ++i) {
+        std::fill(b.row_doc.begin() + b.start[i], b.row_doc.begin() + b.start[i] + b.len[i], i);
+        std::fill(b.brow_doc.begin() + b.bstart[i], b.brow_doc.begin() + b.bstart[i] + b.blen[i], i);
+    }
+    if (tokens_on_host) {
+        for (int i = 0; i < b.T; ++i) {
+            if (tokens[i] < 0 || tokens[i] >= c.hp.n_vocab) {
+                fprintf(stderr, "nexterabert: token id %d out of range\n", tokens[i]);
+                return 1;
+            }
+        }
+        for (int i = 0; types && c.hp.n_types > 0 && i < b.T; ++i) {
+            if (types[i] < 0 || types[i] >= c.hp.n_types) {
+                fprintf(stderr, "nexterabert: token type id %d out of range\n", types[i]);
+                return 1;
+            }
+        }
+    }
+    float base = c.hp.rope_base;
+    if (c.hp.ntk_train_len > 0 && b.max_len > c.hp.ntk_train_len) {
+        if (n_seqs > 1) {
+            fprintf(stderr, "nexterabert: sequences beyond rope.ntk_train_length must be encoded one at a time\n");
+            return 1;
+        }
+        const double d = c.hp.head_dim;
+        base = (float) ((double) base * std::pow((double) b.max_len / c.hp.ntk_train_len, d / (d - 2.0)));
+    }
+    rope0_base = base;
+    return 0;
+}
+
+bool ensure_rope(nextera_context & c, int which, int n_pos, float base) {
+    if (c.rope_n[which] >= n_pos && c.rope_base_cached[which] == base) return true;
+    const int n = std::max(n_pos, 1);
+    std::vector<float> cs, sn;
+    rope_table(n, base, c.hp.head_dim, cs, sn);
+    if (!c.rope_cos[which].alloc(cs.size() * 4) || !c.rope_sin[which].alloc(sn.size() * 4)) return false;
+    cudaMemcpy(c.rope_cos[which].p, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
+    cudaMemcpy(c.rope_sin[which].p, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
+    c.rope_n[which] = n;
+    c.rope_base_cached[which] = base;
+    return true;
+}
+
+bool ensure_arena(nextera_context & c, const Batch & b) {
+    const hparams & hp = c.hp;
+    const int64_t T = std::max<int64_t>(b.T, 1), C = hp.n_embd, I = hp.n_inter;
+    const int64_t HD = (int64_t) hp.n_head * hp.head_dim, GD = (int64_t) hp.n_kv_head * hp.head_dim;
+    const int64_t wide = std::max<int64_t>(I, HD + 2 * GD);
+    const int64_t nb_C = (C + I8_BLOCK - 1) / I8_BLOCK, nb_W = (std::max(I, C) + I8_BLOCK - 1) / I8_BLOCK;
+    bool ok = c.X.reserve(sizeof(float) * T * C) && c.X2.reserve(sizeof(float) * T * C) &&
+              c.U.reserve(sizeof(float) * T * wide) && c.Fa.reserve(sizeof(float) * T * C) &&
+              c.Fb.reserve(sizeof(float) * T * C) && c.Fc.reserve(sizeof(float) * T * C) &&
+              c.Q1.reserve((size_t) T * std::max(I, C)) && c.Q1s.reserve(sizeof(float) * T * nb_W) &&
+              c.Q2.reserve((size_t) T * C) && c.Q2s.reserve(sizeof(float) * T * nb_C);
+    // staged metadata: row_doc T, brow_doc nb, start / len / bstart / blen per document, tokens T,
+    // types T (each padded to 64 entries), then one SSMax scale per (attention layer, document)
+    const size_t meta = sizeof(int32_t) * ((size_t) 3 * T + (size_t) b.nb + 4 * (size_t) b.n_docs + 8 * 64) +
+                        sizeof(float) * (size_t) b.n_docs * (size_t) std::max(hp.n_layer, 1) + 256;
+    ok = ok && c.meta.reserve(meta);
+    size_t ws = std::max(nxk_attention_workspace(b.len.data(), b.n_docs, -1),
+                         nxk_attention_workspace(b.blen.data(), b.n_docs, -1));
+    ok = ok && c.attn_ws.reserve(std::max<size_t>(ws, 256));
+    ok = ok && c.pooled.reserve(sizeof(float) * (size_t) b.n_docs * C);
+    const size_t stage = meta;
+    if (ok && c.h_stage_bytes < stage) {
+        if (c.h_stage) cudaFreeHost(c.h_stage);
+        c.h_stage = nullptr;
+        c.h_stage_bytes = 0;
+        if (cudaMallocHost(&c.h_stage, stage) != cudaSuccess) {
+            cudaGetLastError();
+            ok = false;
+        } else {
+            c.h_stage_bytes = stage;
+        }
+    }
+    return ok;
+}
+
+// One forward pass.  tokens / types are device pointers when the layout says so.
+int run_encoder(nextera_context & c, const Batch & b, float rope0_base, const int32_t * tokens,
+                const int32_t * types, bool on_host, cudaStream_t s, float * d_hidden_out, float * d_pooled_out,
+                int normalize, float ** hidden_dev) {
+    const hparams & hp = c.hp;
+    const int T = b.T, C = hp.n_embd, H = hp.n_head, G = hp.n_kv_head, D = hp.head_dim;
+    if (!ensure_arena(c, b) || !ensure_rope(c, 0, b.max_len, rope0_base) ||
+        !ensure_rope(c, 1, b.max_len, hp.swa_rope_base)) {
+        fprintf(stderr, "nexterabert: failed to allocate the device buffers for %d tokens\n", T);
+        return 2;
+    }
+    // stage the layout (and host tokens) in pinned memory, one copy to the device
+    int32_t * hs = (int32_t *) c.h_stage;
+    int32_t * dm = c.meta.as<int32_t>();
+    size_t o = 0;
+    auto put = [&](const int32_t * src, size_t n) {
+        const size_t at = o;
+        if (src) memcpy(hs + at, src, n * sizeof(int32_t));
+        o += (n + 63) / 64 * 64;
+        return at;
+    };
+    const size_t o_row = put(b.row_doc.data(), T);
+    const size_t o_brow = put(b.brow_doc.data(), b.nb);
+    const size_t o_start = put(b.start.data(), b.n_docs), o_len = put(b.len.data(), b.n_docs);
+    const size_t o_bstart = put(b.bstart.data(), b.n_docs), o_blen = put(b.blen.data(), b.n_docs);
+    size_t o_tok = 0, o_typ = 0;
+    const bool use_types = types && hp.n_types > 0;
+    if (on_host) {
+        o_tok = put(tokens, T);
+        if (use_types) o_typ = put(types, T);
+    }
+    // SSMax scales per attention layer and document (host math as in the reference)
+    std::vector<int> scale_off(hp.n_layer, -1);
+    float * hsc = (float *) (hs + o);
+    size_t n_sc = 0;
+    const float base_scale = 1.0f / std::sqrt((float) D);
+    const int n_layer = c.debug_n_layers >= 0 ? std::min(c.debug_n_layers, hp.n_layer) : hp.n_layer;
+    Forward fw(c, s);
+    for (int l = 0; l < n_layer; ++l) {
+        if (hp.block_types[l] == MIX_LILY) continue;
+        const std::string pre = "blocks." + std::to_string(l) + ".attn.";
+        const bool swa = hp.block_types[l] == MIX_SWA;
+        scale_off[l] = (int) n_sc;
+        for (int d = 0; d < b.n_docs; ++d) {
+            const int n = hp.block_types[l] == MIX_HRA ? b.blen[d] : b.len[d];
+            hsc[n_sc++] = base_scale * (swa ? 1.0f : fw.ssmax_scale(pre, n));
+        }
+    }
+    const size_t stage_ints = o + n_sc;
+    cudaMemcpyAsync(dm, hs, stage_ints * sizeof(int32_t), cudaMemcpyHostToDevice, s);
+    const float * d_scales = (const float *) (dm + o);
+    Layout L;
+    L.row_doc = dm + o_row;
+    L.brow_doc = dm + o_brow;
+    L.start = dm + o_start;
+    L.len = dm + o_len;
+    L.bstart = dm + o_bstart;
+    L.blen = dm + o_blen;
+    L.tokens = on_host ? dm + o_tok : tokens;
+    L.types = use_types ? (on_host ? dm + o_typ : types) : nullptr;
+
+    float * X = c.X.as<float>(), * X2 = c.X2.as<float>(), * U = c.U.as<float>();
+    float * Fa = c.Fa.as<float>(), * Fb = c.Fb.as<float>(), * Fc = c.Fc.as<float>();
+    int8_t * Q1 = c.Q1.as<int8_t>(), * Q2 = c.Q2.as<int8_t>();
+    float * Q1s = c.Q1s.as<float>(), * Q2s = c.Q2s.as<float>();
+
+    // embedding (+ segment embedding)
+    {
+        const RawTensor & e = c.raw.at("embedding.weight");
+        const RawTensor * tt = use_types ? &c.raw.at("token_type_embeddings.weight") : nullptr;
+        fw.mark(PROF_ROWS);
+        fw.rows(nxk_embed(e.type, e.d.p, (int) e.ne[1], C, L.tokens, T, tt ? tt->type : 0, tt ? tt->d.p : nullptr,
+                          tt ? (int) tt->ne[1] : 0, L.types, X, s), "embed");
+    }
+
+    // attention of a mixer over `rows` rows laid out by (start, len, row_doc)
+    auto attention = [&](const std::string & pre, const int8_t * hq, const float * hsx, int rows,
+                         const int32_t * start, const int32_t * len, const int32_t * row_doc,
+                         const std::vector<int32_t> & h_start, const std::vector<int32_t> & h_len, int rope,
+                         int half, const float * scale, float * y) {
+        float * q = U;
+        float * k = U + (size_t) rows * H * D;
+        float * v = k + (size_t) rows * G * D;
+        fw.linear(pre + "c_q.weight", hq, hsx, rows, nullptr, Fc);
+        fw.mark(PROF_ROWS);
+        fw.rows(nxk_qk_prep(Fc, fw.p(pre + "q_norm.alpha"), fw.p(pre + "q_norm.beta"), c.rope_cos[rope].as<float>(),
+                            c.rope_sin[rope].as<float>(), row_doc, start, rows, H, D, 0, q, s), "qk_prep(q)");
+        fw.linear(pre + "c_k.weight", hq, hsx, rows, nullptr, Fc);
+        fw.mark(PROF_ROWS);
+        fw.rows(nxk_qk_prep(Fc, fw.p(pre + "k_norm.alpha"), fw.p(pre + "k_norm.beta"), c.rope_cos[rope].as<float>(),
+                            c.rope_sin[rope].as<float>(), row_doc, start, rows, G, D, 1, k, s), "qk_prep(k)");
+        fw.linear(pre + "c_v.weight", hq, hsx, rows, nullptr, Fc);
+        fw.mark(PROF_ROWS);
+        fw.rows(nxk_head_major(Fc, rows, G, D, v, s), "head_major");
+        fw.mark(PROF_ATTN);
+        fw.rows(nxk_attention(q, k, v, rows, H, G, D, half, scale, row_doc, start, len, b.n_docs, h_start.data(),
+                              h_len.data(), c.attn_ws.p, c.attn_ws.bytes, y, s), "attention");
+    };
+
+    // x + c_proj(sigmoid(c_gate(y)) * z)  (gated_out, :1209-1214); y, z: [T][C]
+    auto gated_out = [&](const std::string & pre, const float * y, const float * z, float * gl) {
+        fw.mark(PROF_ROWS);
+        fw.rows(nxk_quantize(y, T, C, Q1, Q1s, s), "quantize");
+        fw.linear(pre + "c_gate.weight", Q1, Q1s, T, nullptr, gl);
+        fw.mark(PROF_ROWS);
+        fw.rows(nxk_gate(gl, z, T, C, nullptr, Q1, Q1s, s), "gate");
+        fw.linear(pre + "c_proj.weight", Q1, Q1s, T, X, X2);
+        std::swap(X, X2);
+    };
+
+    for (int l = 0; l < n_layer && fw.ok; ++l) {
+        const std::string blk = "blocks." + std::to_string(l) + ".", pre = blk + "attn.";
+        const mixer_type mt = hp.block_types[l];
+        fw.mark(PROF_ROWS);
+        fw.rows(nxk_rms_norm(X, fw.p(blk + "attn_norm.weight"), hp.rms_eps, T, C, nullptr, Q2, Q2s, s), "rms_norm");
+        if (mt == MIX_LILY) {
+            const int r = fw.n_out(pre + "ltc_conv.in_proj.weight");
+            fw.linear(pre + "ltc_conv.in_proj.weight", Q2, Q2s, T, nullptr, Fa);
+            fw.linear(pre + "ltc_conv.A.weight", Q2, Q2s, T, nullptr, Fb);
+            const ConvTaps * k1 = fw.taps(pre + "ltc_conv.kernel");
+            if (!fw.ok) break;
+            fw.mark(PROF_ROWS);
+            fw.rows(nxk_dwconv(Fa, Fb, k1->taps.as<float>(), k1->k, L.row_doc, L.start, L.len, T, r, nullptr, Q1, Q1s, s),
+                    "dwconv");
+            fw.linear(pre + "ltc_conv.out_proj.weight", Q1, Q1s, T, nullptr, Fa);
+            fw.linear(pre + "x_proj.weight", Q2, Q2s, T, nullptr, Fb);
+            fw.linear(pre + "B_proj.weight", Q2, Q2s, T, nullptr, Fc);
+            const ConvTaps * k2 = fw.taps(pre + "state_conv.depthwise.weight");
+            if (!fw.ok) break;
+            fw.mark(PROF_ROWS);
+            fw.rows(nxk_lily_state(Fa, Fb, Fc, k2->taps.as<float>(), k2->k, L.row_doc, L.start, L.len, T, C, nullptr,
+                                   Q1, Q1s, s), "lily_state");
+            fw.linear(pre + "c_proj.weight", Q1, Q1s, T, X, X2);
+            std::swap(X, X2);
+        } else if (mt == MIX_SWA || mt == MIX_ATTN) {
+            const bool swa = mt == MIX_SWA;
+            const int half = swa ? std::max(1, hp.swa_window / 2) : -1;
+            attention(pre, Q2, Q2s, T, L.start, L.len, L.row_doc, b.start, b.len, swa ? 1 : 0, half,
+                      d_scales + scale_off[l], Fb);
+            gated_out(pre, Fb, Fb, Fa);
+        } else {
+            // HRA (mix_hra, :1246-1264)
+            fw.linear(pre + "qkv_in.weight", Q2, Q2s, T, nullptr, Fa);
+            const ConvTaps * kq = fw.taps(pre + "qkv_conv.depthwise.weight");
+            if (!fw.ok) break;
+            fw.mark(PROF_ROWS);
+            fw.rows(nxk_dwconv(Fa, nullptr, kq->taps.as<float>(), kq->k, L.row_doc, L.start, L.len, T, C, Fb, nullptr,
+                               nullptr, s), "dwconv");
+            fw.linear(pre + "qkv_gate.weight", Q2, Q2s, T, nullptr, Fa);
+            fw.mark(PROF_ROWS);
+            fw.rows(nxk_block_mean(Fb, Fa, C, hp.hra_block, L.start, L.len, L.bstart, L.brow_doc, b.nb, nullptr, Q1, Q1s,
+                                   s), "block_mean");
+            attention(pre, Q1, Q1s, b.nb, L.bstart, L.blen, L.brow_doc, b.bstart, b.blen, 0, -1,
+                      d_scales + scale_off[l], Fa);
+            fw.linear(pre + "c_C.weight", Q2, Q2s, T, nullptr, Fb);
+            fw.mark(PROF_ROWS);
+            fw.rows(nxk_upsample_add(Fa, Fb, C, hp.hra_block, T, L.row_doc, L.start, L.bstart, Fc, s), "upsample_add");
+            const ConvTaps * ko = fw.taps(pre + "c_o.depthwise.weight");
+            if (!fw.ok) break;
+            fw.mark(PROF_ROWS);
+            fw.rows(nxk_dwconv(Fc, nullptr, ko->taps.as<float>(), ko->k, L.row_doc, L.start, L.len, T, C, Fb, nullptr,
+                               nullptr, s), "dwconv");
+            gated_out(pre, Fc, Fb, Fa);
+        }
+        // MLP (:1284-1289)
+        fw.mark(PROF_ROWS);
+        fw.rows(nxk_rms_norm(X, fw.p(blk + "mlp_norm.weight"), hp.rms_eps, T, C, nullptr, Q2, Q2s, s), "rms_norm");
+        const int I = fw.n_out(blk + "mlp.c_fc.weight");
+        fw.linear(blk + "mlp.c_fc.weight", Q2, Q2s, T, nullptr, U);
+        fw.mark(PROF_ROWS);
+        fw.rows(nxk_relu_sqr(U, T, I, nullptr, Q1, Q1s, s), "relu_sqr");
+        fw.linear(blk + "mlp.c_proj.weight", Q1, Q1s, T, X, X2);
+        std::swap(X, X2);
+    }
+    if (!fw.ok) return 3;
+    float * hidden = X;
+    if (c.debug_n_layers < 0) {
+        fw.mark(PROF_ROWS);
+        fw.rows(nxk_layer_norm(X, fw.p("out_norm.weight"), fw.p("out_norm.bias"), hp.ln_eps, T, C, X2, s), "layer_norm");
+        hidden = X2;
+    }
+    float * pooled = d_pooled_out ? d_pooled_out : c.pooled.as<float>();
+    fw.mark(PROF_ROWS);
+    fw.rows(nxk_pool(hidden, L.start, L.len, b.n_docs, C, normalize, pooled, s), "pool");
+    if (d_hidden_out) cudaMemcpyAsync(d_hidden_out, hidden, sizeof(float) * (size_t) T * C, cudaMemcpyDeviceToDevice, s);
+    fw.mark(-1);
+    if (!fw.ok) return 3;
+    *hidden_dev = hidden;
+    return 0;
+}
+
+void collect_profile(nextera_context & c) {
+    profiler & pr = c.prof;
+    if (!pr.enabled || pr.marks.size() < 2) return;
+    cudaEventSynchronize(pr.marks.back().first);
+    for (size_t i = 0; i + 1 < pr.marks.size(); ++i) {
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, pr.marks[i].first, pr.marks[i + 1].first);
+        if (pr.marks[i].second >= 0) pr.ms[pr.marks[i].second] += ms;
+    }
+    for (auto & m : pr.marks) cudaEventDestroy(m.first);
+    pr.marks.clear();
+}
+
+int32_t encode_host(nextera_context * c, const int32_t * tokens, const int32_t * types, const int32_t * lengths,
+                    int32_t n_seqs, float * hidden, float * pooled, int32_t normalize) {
+    const auto t0 = std::chrono::steady_clock::now();
+    cudaSetDevice(c->device);
+    Batch b;
+    float rope0 = 0.0f;
+    if (!tokens) return 1;
+    int rc = prepare(*c, tokens, types, lengths, n_seqs, true, b, rope0);
+    if (rc) return rc;
+    float * hid = nullptr;
+    rc = run_encoder(*c, b, rope0, tokens, types, true, c->stream, nullptr, nullptr, normalize, &hid);
+    if (rc == 0) {
+        if (hidden) cudaMemcpyAsync(hidden, hid, sizeof(float) * (size_t) b.T * c->hp.n_embd, cudaMemcpyDeviceToHost, c->stream);
+        if (pooled) cudaMemcpyAsync(pooled, c->pooled.p, sizeof(float) * (size_t) n_seqs * c->hp.n_embd,
+                                    cudaMemcpyDeviceToHost, c->stream);
+        if (cudaStreamSynchronize(c->stream) != cudaSuccess) {
+            fprintf(stderr, "nexterabert: device error: %s\n", cudaGetErrorString(cudaGetLastError()));
+            rc = 3;
+        } else if (int32_t e = nxk_take_error(c->stream)) {
+            fprintf(stderr, "nexterabert: a kernel timed out waiting on its pipeline (code 0x%x)\n", e);
+            rc = 3;
+        }
+    }
+    collect_profile(*c);
+    c->last_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    if (c->prof.enabled) {
+        c->prof.total_ms += c->last_ms;
+        c->prof.calls++;
+    }
+    return rc;
+}
+
+} // namespace
+
+int32_t nextera_encode(struct nextera_context * c, const int32_t * tokens, const int32_t * lengths, int32_t n_seqs,
+                       float * hidden, float * pooled, int32_t normalize) {
+    return encode_host(c, tokens, nullptr, lengths, n_seqs, hidden, pooled, normalize);
+}
+
+int32_t nextera_encode_segments(struct nextera_context * c, const int32_t * tokens, const int32_t * token_types,
+                                const int32_t * lengths, int32_t n_seqs, float * hidden, float * pooled,
+                                int32_t normalize) {
+    return encode_host(c, tokens, token_types, lengths, n_seqs, hidden, pooled, normalize);
+}
+
+int32_t nextera_encode_device(struct nextera_context * c, const int32_t * d_tokens, const int32_t * d_token_types,
+                              const int32_t * lengths, int32_t n_seqs, float * d_hidden, float * d_pooled,
+                              int32_t normalize, void * stream) {
+    cudaSetDevice(c->device);
+    Batch b;
+    float rope0 = 0.0f;
+    if (!d_tokens) return 1;
+    int rc = prepare(*c, nullptr, nullptr, lengths, n_seqs, false, b, rope0);
+    if (rc) return rc;
+    float * hid = nullptr;
+    return run_encoder(*c, b, rope0, d_tokens, d_token_types, false, (cudaStream_t) stream, d_hidden, d_pooled,
+                       normalize, &hid);
+}
+
+int32_t nextera_pooler_output(struct nextera_context * c, const int32_t *, const int32_t *, const int32_t *, int32_t,
+                              float *) {
+    if (!c->hp.has_pooler) {
+        fprintf(stderr, "nexterabert: this file has no pooler\n");
+        return 1;
+    }
+    fprintf(stderr, "nexterabert: pooler_output is not available on the GPU path of this build\n");
+    return 1;
+}
+
+int32_t nextera_classify(struct nextera_context * c, const int32_t *, const int32_t *, const int32_t *, int32_t,
+                         float *) {
+    if (c->hp.cls == CLS_NONE) {
+        fprintf(stderr, "nexterabert: this file has no classifier head\n");
+        return 1;
+    }
+    fprintf(stderr, "nexterabert: classify is not available on the GPU path of this build\n");
+    return 1;
+}
+
+int32_t nextera_mlm_logits(struct nextera_context * c, const int32_t *, int32_t, const int32_t *, int32_t, float *) {
+    if (!c->hp.has_mlm) {
+        fprintf(stderr, "nexterabert: this file has no MLM head\n");
+        return 1;
+    }
+    fprintf(stderr, "nexterabert: mlm_logits is not available on the GPU path of this build\n");
+    return 1;
+}

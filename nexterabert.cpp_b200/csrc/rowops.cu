@@ -1,0 +1,527 @@
+// Row ops, activation quantization, embedding gather, weight expansion,
+// LayerNorm and pooling for sm_100a.
+//
+// All of these are HBM-bound.  The layout is one warp per row: lane L owns the
+// elements 32*i + L, so every load and store of a warp is one contiguous
+// 128-byte segment, and the lane's fma chain over those elements is exactly
+// one lane of the reference's 32-lane dot_f32 accumulator (src/nexterabert.cpp
+// :133-151).  Rows are produced element by element in the reference's
+// operation order and, when the consumer is an int8 linear, quantized per
+// (row, 256-column block) in the same pass (quantize_row, :378-403): the fp32
+// row never touches memory.
+#include "common.cuh"
+#include "dequant.cuh"
+#include "nextera_kernels.h"
+
+#include <cuda_runtime.h>
+
+namespace nxk {
+
+__device__ int g_error;
+
+constexpr int ROW_THREADS = 256;     // 8 rows per block
+
+// ---------------------------------------------------------------------------
+// generic row emitter: fp32 output, or int8 codes + per-block scales
+// ---------------------------------------------------------------------------
+template <class Op>
+__global__ void __launch_bounds__(ROW_THREADS) row_kernel(Op op, int T, int C, float * __restrict__ out,
+                                                          int8_t * __restrict__ q, float * __restrict__ sx) {
+    const int t = (int) ((blockIdx.x * (size_t) blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
+    if (t >= T) return;
+    op.prepare(t, lane, C);
+    const int n_i = C >> 5;
+    if (!q) {
+        float * o = out + (size_t) t * C;
+        for (int i = 0; i < n_i; ++i) o[32 * i + lane] = op.value(t, 32 * i + lane, C);
+        return;
+    }
+    const int n_blk = (C + I8_BLOCK - 1) / I8_BLOCK;
+    int8_t * qo = q + (size_t) t * C;
+    for (int B = 0; B < n_blk; ++B) {
+        float v[8];
+        float am = 0.0f;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = 8 * B + u;
+            v[u] = i < n_i ? op.value(t, 32 * i + lane, C) : 0.0f;
+            am = fmaxf(am, fabsf(v[u]));
+        }
+        am = warp_max(am);
+        const float inv = act_inv(am);
+        if (lane == 0) sx[(size_t) t * n_blk + B] = act_scale(am);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = 8 * B + u;
+            if (i < n_i) qo[32 * i + lane] = act_code(v[u], inv);
+        }
+    }
+}
+
+struct CopyOp {
+    const float * x;
+    __device__ void prepare(int, int, int) {}
+    __device__ float value(int t, int c, int C) const { return x[(size_t) t * C + c]; }
+};
+
+// op_rms_norm (:464-482): x * (1 / sqrt(dot(x, x) / C + eps)) * g
+struct RmsOp {
+    const float * x;
+    const float * g;
+    float eps;
+    float inv;
+    __device__ void prepare(int t, int lane, int C) {
+        const float * xr = x + (size_t) t * C;
+        float acc = 0.0f;
+        for (int i = 0; i < (C >> 5); ++i) {
+            const float v = xr[32 * i + lane];
+            acc = __fmaf_rn(v, v, acc);
+        }
+        const float dot = warp_dot_tree(acc);
+        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(dot, (float) C), eps)));
+    }
+    __device__ float value(int t, int c, int C) const {
+        return __fmul_rn(__fmul_rn(x[(size_t) t * C + c], inv), g[c]);
+    }
+};
+
+// op_relu_sqr (:485-505)
+struct ReluSqrOp {
+    const float * x;
+    __device__ void prepare(int, int, int) {}
+    __device__ float value(int t, int c, int C) const {
+        const float v = x[(size_t) t * C + c];
+        const float r = v > 0.0f ? v : 0.0f;
+        return __fmul_rn(r, r);
+    }
+};
+
+// op_gate (:508-523): sigmoid(g) * y
+struct GateOp {
+    const float * g;
+    const float * y;
+    __device__ void prepare(int, int, int) {}
+    __device__ float value(int t, int c, int C) const {
+        const size_t i = (size_t) t * C + c;
+        return __fmul_rn(sigmoid8(g[i]), y[i]);
+    }
+};
+
+// op_dwconv (:528-544): r (or 0) + sum_j w[j][c] * x[t + j - k/2][c] inside the document
+struct DwconvOp {
+    const float * x;
+    const float * r;
+    const float * taps;
+    int k;
+    const int32_t * row_doc;
+    const int32_t * doc_start;
+    const int32_t * doc_len;
+    int lo, hi;
+    __device__ void prepare(int t, int, int) {
+        const int d = row_doc[t];
+        lo = doc_start[d];
+        hi = lo + doc_len[d];
+    }
+    __device__ float value(int t, int c, int C) const {
+        float v = r ? r[(size_t) t * C + c] : 0.0f;
+        for (int j = 0; j < k; ++j) {
+            const int tt = t + j - k / 2;
+            if (tt < lo || tt >= hi) continue;
+            v = __fmaf_rn(taps[(size_t) j * C + c], x[(size_t) tt * C + c], v);
+        }
+        return v;
+    }
+};
+
+// op_lily_state (:548-579): b[t] * sum_j w[j] * (a * x)[t + j - k/2]
+struct LilyOp {
+    const float * a;
+    const float * x;
+    const float * b;
+    const float * taps;
+    int k;
+    const int32_t * row_doc;
+    const int32_t * doc_start;
+    const int32_t * doc_len;
+    int j0, j1;
+    __device__ void prepare(int t, int, int) {
+        const int d = row_doc[t];
+        const int lo = doc_start[d], hi = lo + doc_len[d];
+        j0 = max(0, lo - (t - k / 2));
+        j1 = min(k, hi - (t - k / 2));
+    }
+    __device__ float value(int t, int c, int C) const {
+        float acc = 0.0f;
+        for (int j = j0; j < j1; ++j) {
+            const size_t tt = (size_t) (t + j - k / 2) * C + c;
+            acc = __fmaf_rn(taps[(size_t) j * C + c], __fmul_rn(a[tt], x[tt]), acc);
+        }
+        return __fmul_rn(acc, b[(size_t) t * C + c]);
+    }
+};
+
+// op_block_mean (:642-660): mean over each HRA block's real tokens of h (* g)
+struct BlockMeanOp {
+    const float * h;
+    const float * g;
+    int block;
+    const int32_t * doc_start;
+    const int32_t * doc_len;
+    const int32_t * bdoc_start;
+    const int32_t * brow_doc;
+    int ts, n;
+    float inv;
+    __device__ void prepare(int b, int, int) {
+        const int d = brow_doc[b], bi = b - bdoc_start[d];
+        ts = doc_start[d] + bi * block;
+        n = min(block, doc_len[d] - bi * block);
+        inv = __fdiv_rn(1.0f, (float) n);
+    }
+    __device__ float value(int, int c, int C) const {
+        float acc = 0.0f;
+        for (int i = 0; i < n; ++i) {
+            const size_t at = (size_t) (ts + i) * C + c;
+            acc = g ? __fmaf_rn(h[at], g[at], acc) : __fmaf_rn(1.0f, h[at], acc);
+        }
+        return __fmul_rn(acc, inv);
+    }
+};
+
+// op_upsample_add (:679-690)
+struct UpsampleOp {
+    const float * y;
+    const float * r;
+    int block;
+    const int32_t * row_doc;
+    const int32_t * doc_start;
+    const int32_t * bdoc_start;
+    int yb;
+    __device__ void prepare(int t, int, int) {
+        const int d = row_doc[t];
+        yb = bdoc_start[d] + (t - doc_start[d]) / block;
+    }
+    __device__ float value(int t, int c, int C) const {
+        return __fadd_rn(y[(size_t) yb * C + c], r[(size_t) t * C + c]);
+    }
+};
+
+template <class Op>
+int launch_rows(const Op & op, int T, int C, float * out, int8_t * q, float * sx, cudaStream_t s) {
+    if (T < 0 || C <= 0 || (C & 31) || (!q && !out) || (q && !sx)) return NXK_EINVAL;
+    if (T == 0) return NXK_OK;
+    const int rows_per_block = ROW_THREADS / 32;
+    const unsigned grid = (unsigned) ((T + rows_per_block - 1) / rows_per_block);
+    row_kernel<Op><<<grid, ROW_THREADS, 0, s>>>(op, T, C, out, q, sx);
+    return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
+}
+
+// ---------------------------------------------------------------------------
+// qk_prep (:590-625): DyT then RoPE at the document-relative position.
+// One warp per (row, head); lane i owns the pair (i, i + D/2).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) qk_prep_kernel(const float * __restrict__ x, const float * __restrict__ alpha,
+                                                      const float * __restrict__ beta, const float * __restrict__ cos_t,
+                                                      const float * __restrict__ sin_t, const int32_t * __restrict__ row_doc,
+                                                      const int32_t * __restrict__ doc_start, int T, int H, int D,
+                                                      int head_major, float * __restrict__ out) {
+    const size_t w = (blockIdx.x * (size_t) blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (w >= (size_t) T * H) return;
+    const int t = (int) (w / H), h = (int) (w % H);
+    const int half = D >> 1;
+    const int pos = t - doc_start[row_doc[t]];
+    const float * x1 = x + (size_t) t * H * D + (size_t) h * D;
+    float * y1 = head_major ? out + ((size_t) h * T + t) * D : out + (size_t) t * H * D + (size_t) h * D;
+    for (int i = lane; i < half; i += 32) {
+        const float c = cos_t[(size_t) pos * half + i], s = sin_t[(size_t) pos * half + i];
+        const float a = __fmul_rn(beta[i], tanh8(__fmul_rn(alpha[i], x1[i])));
+        const float b = __fmul_rn(beta[half + i], tanh8(__fmul_rn(alpha[half + i], x1[half + i])));
+        y1[i] = __fmaf_rn(a, c, __fmul_rn(b, s));
+        y1[half + i] = __fmaf_rn(-a, s, __fmul_rn(b, c));
+    }
+}
+
+__global__ void head_major_kernel(const float * __restrict__ x, int T, int H, int D, float * __restrict__ out) {
+    const size_t i = blockIdx.x * (size_t) blockDim.x + threadIdx.x;
+    const size_t n = (size_t) T * H * D;
+    if (i >= n) return;
+    const int d = (int) (i % D);
+    const size_t th = i / D;
+    const int h = (int) (th % H), t = (int) (th / H);
+    out[((size_t) h * T + t) * D + d] = x[i];
+}
+
+// ---------------------------------------------------------------------------
+// LayerNorm (ggml_norm restated: mean and variance accumulated in double) * w + b
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ double warp_sum_d(double v) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__global__ void __launch_bounds__(256) layer_norm_kernel(const float * __restrict__ x, const float * __restrict__ w,
+                                                         const float * __restrict__ b, float eps, int T, int C,
+                                                         float * __restrict__ out) {
+    const int t = (int) ((blockIdx.x * (size_t) blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
+    if (t >= T) return;
+    const float * xr = x + (size_t) t * C;
+    double s = 0.0;
+    for (int c = lane; c < C; c += 32) s += (double) xr[c];
+    const float mean = (float) (warp_sum_d(s) / C);
+    double s2 = 0.0;
+    for (int c = lane; c < C; c += 32) {
+        const float v = __fsub_rn(xr[c], mean);
+        s2 += (double) __fmul_rn(v, v);
+    }
+    const float variance = (float) (warp_sum_d(s2) / C);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(variance, eps)));
+    float * o = out + (size_t) t * C;
+    for (int c = lane; c < C; c += 32) {
+        float y = __fmul_rn(__fsub_rn(xr[c], mean), scale);
+        if (w) y = __fmul_rn(y, w[c]);
+        if (b) y = __fadd_rn(y, b[c]);
+        o[c] = y;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// pooling (:1903-1918): per (document, channel) sequential sum, then the scale
+// ---------------------------------------------------------------------------
+__global__ void pool_sum_kernel(const float * __restrict__ hidden, const int32_t * __restrict__ doc_start,
+                                const int32_t * __restrict__ doc_len, int n_docs, int C, float * __restrict__ pooled) {
+    const size_t i = blockIdx.x * (size_t) blockDim.x + threadIdx.x;
+    if (i >= (size_t) n_docs * C) return;
+    const int d = (int) (i / C), c = (int) (i % C);
+    const float * h = hidden + (size_t) doc_start[d] * C + c;
+    const int n = doc_len[d];
+    float s = 0.0f;
+    int t = 0;
+    for (; t + 4 <= n; t += 4) {       // loads issued together, adds kept in order
+        const float a0 = h[(size_t) t * C], a1 = h[(size_t) (t + 1) * C];
+        const float a2 = h[(size_t) (t + 2) * C], a3 = h[(size_t) (t + 3) * C];
+        s = __fadd_rn(s, a0);
+        s = __fadd_rn(s, a1);
+        s = __fadd_rn(s, a2);
+        s = __fadd_rn(s, a3);
+    }
+    for (; t < n; ++t) s = __fadd_rn(s, h[(size_t) t * C]);
+    pooled[i] = s;
+}
+
+__global__ void pool_scale_kernel(const int32_t * __restrict__ doc_len, int n_docs, int C, int normalize,
+                                  float * __restrict__ pooled) {
+    const int d = (int) ((blockIdx.x * (size_t) blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
+    if (d >= n_docs) return;
+    float * pv = pooled + (size_t) d * C;
+    float scale = __fdiv_rn(1.0f, (float) doc_len[d]);
+    if (normalize) {
+        float acc = 0.0f;
+        for (int i = 0; i < (C >> 5); ++i) {
+            const float v = pv[32 * i + lane];
+            acc = __fmaf_rn(v, v, acc);
+        }
+        const float nrm = __fsqrt_rn(warp_dot_tree(acc));
+        scale = nrm > 0.0f ? __fdiv_rn(1.0f, nrm) : 0.0f;
+    }
+    for (int c = lane; c < C; c += 32) pv[c] = __fmul_rn(pv[c], scale);
+}
+
+// ---------------------------------------------------------------------------
+// embedding rows (get_rows + add of the segment embedding)
+// ---------------------------------------------------------------------------
+constexpr int ERR_TOKEN_RANGE = 0x201;
+
+__global__ void embed_kernel(int type, const uint8_t * __restrict__ table, size_t row_bytes, int n_rows, int C,
+                             const int32_t * __restrict__ tokens, int T, int ttype, const uint8_t * __restrict__ ttable,
+                             size_t trow_bytes, int tn_rows, const int32_t * __restrict__ types,
+                             float * __restrict__ out) {
+    const size_t i = blockIdx.x * (size_t) blockDim.x + threadIdx.x;
+    if (i >= (size_t) T * C) return;
+    const int t = (int) (i / C), c = (int) (i % C);
+    const int id = tokens[t];
+    if (id < 0 || id >= n_rows) {
+        out[i] = 0.0f;
+        if (c == 0) atomicExch(&g_error, ERR_TOKEN_RANGE);
+        return;
+    }
+    float v = deq_elem(type, table + row_bytes * (size_t) id, c);
+    if (ttable) {
+        const int ty = types[t];
+        if (ty < 0 || ty >= tn_rows) {
+            if (c == 0) atomicExch(&g_error, ERR_TOKEN_RANGE);
+        } else {
+            v = __fadd_rn(v, deq_elem(ttype, ttable + trow_bytes * (size_t) ty, c));
+        }
+    }
+    out[i] = v;
+}
+
+// ---------------------------------------------------------------------------
+// build_i8_weight (:1010-1049): one warp per (row, 256-block)
+// ---------------------------------------------------------------------------
+__global__ void expand_kernel(int type, const uint8_t * __restrict__ blocks, size_t row_bytes, int n_in, int n_out,
+                              int8_t * __restrict__ w8, float * __restrict__ scale, int32_t * __restrict__ off) {
+    const size_t wi = (blockIdx.x * (size_t) blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int n_blk = (n_in + I8_BLOCK - 1) / I8_BLOCK;
+    if (wi >= (size_t) n_out * n_blk) return;
+    const int r = (int) (wi / n_blk), B = (int) (wi % n_blk);
+    const uint8_t * row = blocks + row_bytes * (size_t) r;
+    float v[8];
+    float am = 0.0f;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+        const int e = B * I8_BLOCK + 32 * u + lane;
+        v[u] = e < n_in ? deq_elem(type, row, e) : 0.0f;
+        am = fmaxf(am, fabsf(v[u]));
+    }
+    am = warp_max(am);
+    const float inv = am > 0.0f ? __fdiv_rn(127.0f, am) : 0.0f;
+    int sum = 0;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+        const int e = B * I8_BLOCK + 32 * u + lane;
+        if (e < n_in) {
+            const int qv = (int) roundf(__fmul_rn(v[u], inv));      // lround: half away from zero
+            w8[(size_t) r * n_in + e] = (int8_t) qv;
+            sum += qv;
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) {
+        scale[(size_t) B * n_out + r] = __fdiv_rn(am, 127.0f);
+        if (off) off[(size_t) B * n_out + r] = -128 * sum;
+    }
+}
+
+} // namespace nxk
+
+using namespace nxk;
+
+static inline cudaStream_t S(void * s) { return (cudaStream_t) s; }
+static inline int launched() { return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH; }
+
+extern "C" {
+
+int32_t nxk_take_error(void * stream) {
+    int v = 0, zero = 0;
+    cudaStreamSynchronize(S(stream));
+    cudaMemcpyFromSymbol(&v, g_error, sizeof(int));
+    cudaMemcpyToSymbol(g_error, &zero, sizeof(int));
+    return v;
+}
+
+int nxk_quantize(const float * x, int T, int C, int8_t * q, float * sx, void * stream) {
+    return launch_rows(CopyOp{x}, T, C, nullptr, q, sx, S(stream));
+}
+
+int nxk_rms_norm(const float * x, const float * gain, float eps, int T, int C, float * out, int8_t * q, float * sx,
+                 void * stream) {
+    return launch_rows(RmsOp{x, gain, eps, 0.0f}, T, C, out, q, sx, S(stream));
+}
+
+int nxk_relu_sqr(const float * x, int T, int C, float * out, int8_t * q, float * sx, void * stream) {
+    return launch_rows(ReluSqrOp{x}, T, C, out, q, sx, S(stream));
+}
+
+int nxk_gate(const float * g, const float * y, int T, int C, float * out, int8_t * q, float * sx, void * stream) {
+    return launch_rows(GateOp{g, y}, T, C, out, q, sx, S(stream));
+}
+
+int nxk_dwconv(const float * x, const float * r, const float * taps, int k, const int32_t * row_doc,
+               const int32_t * doc_start, const int32_t * doc_len, int T, int C, float * out, int8_t * q,
+               float * sx, void * stream) {
+    if (k <= 0) return NXK_EINVAL;
+    return launch_rows(DwconvOp{x, r, taps, k, row_doc, doc_start, doc_len, 0, 0}, T, C, out, q, sx, S(stream));
+}
+
+int nxk_lily_state(const float * a, const float * x, const float * b, const float * taps, int k,
+                   const int32_t * row_doc, const int32_t * doc_start, const int32_t * doc_len, int T, int C,
+                   float * out, int8_t * q, float * sx, void * stream) {
+    if (k <= 0) return NXK_EINVAL;
+    return launch_rows(LilyOp{a, x, b, taps, k, row_doc, doc_start, doc_len, 0, 0}, T, C, out, q, sx, S(stream));
+}
+
+int nxk_block_mean(const float * h, const float * g, int C, int block, const int32_t * doc_start,
+                   const int32_t * doc_len, const int32_t * bdoc_start, const int32_t * brow_doc, int n_brows,
+                   float * out, int8_t * q, float * sx, void * stream) {
+    if (block <= 0) return NXK_EINVAL;
+    return launch_rows(BlockMeanOp{h, g, block, doc_start, doc_len, bdoc_start, brow_doc, 0, 0, 0.0f},
+                       n_brows, C, out, q, sx, S(stream));
+}
+
+int nxk_upsample_add(const float * y, const float * r, int C, int block, int T, const int32_t * row_doc,
+                     const int32_t * doc_start, const int32_t * bdoc_start, float * out, void * stream) {
+    if (block <= 0) return NXK_EINVAL;
+    return launch_rows(UpsampleOp{y, r, block, row_doc, doc_start, bdoc_start, 0}, T, C, out, nullptr, nullptr,
+                       S(stream));
+}
+
+int nxk_qk_prep(const float * x, const float * alpha, const float * beta, const float * cos_t, const float * sin_t,
+                const int32_t * row_doc, const int32_t * doc_start, int T, int H, int D, int head_major, float * out,
+                void * stream) {
+    if (T < 0 || H <= 0 || D <= 0 || (D & 1)) return NXK_EINVAL;
+    if (T == 0) return NXK_OK;
+    const size_t warps = (size_t) T * H;
+    qk_prep_kernel<<<(unsigned) ((warps * 32 + 255) / 256), 256, 0, S(stream)>>>(
+        x, alpha, beta, cos_t, sin_t, row_doc, doc_start, T, H, D, head_major, out);
+    return launched();
+}
+
+int nxk_head_major(const float * x, int T, int H, int D, float * out, void * stream) {
+    if (T < 0 || H <= 0 || D <= 0) return NXK_EINVAL;
+    const size_t n = (size_t) T * H * D;
+    if (!n) return NXK_OK;
+    head_major_kernel<<<(unsigned) ((n + 255) / 256), 256, 0, S(stream)>>>(x, T, H, D, out);
+    return launched();
+}
+
+int nxk_layer_norm(const float * x, const float * w, const float * b, float eps, int T, int C, float * out,
+                   void * stream) {
+    if (T < 0 || C <= 0) return NXK_EINVAL;
+    if (T == 0) return NXK_OK;
+    layer_norm_kernel<<<(unsigned) ((T + 7) / 8), 256, 0, S(stream)>>>(x, w, b, eps, T, C, out);
+    return launched();
+}
+
+int nxk_pool(const float * hidden, const int32_t * doc_start, const int32_t * doc_len, int n_docs, int C,
+             int normalize, float * pooled, void * stream) {
+    if (n_docs < 0 || C <= 0 || (C & 31)) return NXK_EINVAL;
+    if (n_docs == 0) return NXK_OK;
+    const size_t n = (size_t) n_docs * C;
+    pool_sum_kernel<<<(unsigned) ((n + 255) / 256), 256, 0, S(stream)>>>(hidden, doc_start, doc_len, n_docs, C, pooled);
+    pool_scale_kernel<<<(unsigned) ((n_docs + 7) / 8), 256, 0, S(stream)>>>(doc_len, n_docs, C, normalize, pooled);
+    return launched();
+}
+
+int nxk_embed(int type, const void * table, int n_rows, int C, const int32_t * tokens, int T, int ttype,
+              const void * ttable, int tn_rows, const int32_t * types, float * out, void * stream) {
+    const int bs = blck_size(type);
+    if (T < 0 || C <= 0 || n_rows <= 0 || bs <= 0 || C % bs) return NXK_EINVAL;
+    if (ttable && (blck_size(ttype) <= 0 || C % blck_size(ttype) || !types)) return NXK_EINVAL;
+    if (T == 0) return NXK_OK;
+    const size_t rb = (size_t) (C / bs) * type_size(type);
+    const size_t trb = ttable ? (size_t) (C / blck_size(ttype)) * type_size(ttype) : 0;
+    const size_t n = (size_t) T * C;
+    embed_kernel<<<(unsigned) ((n + 255) / 256), 256, 0, S(stream)>>>(
+        type, (const uint8_t *) table, rb, n_rows, C, tokens, T, ttype, (const uint8_t *) ttable, trb, tn_rows, types,
+        out);
+    return launched();
+}
+
+int nxk_expand_weight(int type, const void * blocks, int n_in, int n_out, int8_t * w8, float * scale, int32_t * off,
+                      void * stream) {
+    const int bs = blck_size(type);
+    if (n_in <= 0 || n_out <= 0 || bs <= 0 || n_in % bs) return NXK_EINVAL;
+    const size_t rb = (size_t) (n_in / bs) * type_size(type);
+    const int n_blk = (n_in + I8_BLOCK - 1) / I8_BLOCK;
+    const size_t warps = (size_t) n_out * n_blk;
+    expand_kernel<<<(unsigned) ((warps * 32 + 255) / 256), 256, 0, S(stream)>>>(
+        type, (const uint8_t *) blocks, rb, n_in, n_out, w8, scale, off);
+    return launched();
+}
+
+} // extern "C"
