@@ -1,20 +1,33 @@
-// Grouped-query attention over a packed, unpadded batch of documents.
+// Grouped-query attention over a packed, unpadded batch of documents,
+// reproducing the reference's op_attention (src/nexterabert.cpp:698-852)
+// operation for operation.
 //
-// Computes what the reference's op_attention (src/nexterabert.cpp:785-852)
-// computes -- for every query row t and head h, softmax(scale[doc] * q . k) over
-// the keys of t's document (optionally only those with |i - j| <= half) applied
-// to v -- without materialising the score matrix: keys are streamed through
-// shared memory in tiles and the softmax is accumulated online (running max and
-// sum, rescaled per tile).  All arithmetic is fp32; results agree with the
-// reference's two-pass softmax to ~1e-6 relative (different summation order and
-// exp implementation), checked against the oracle at 1e-4.
+// Why exact: every linear layer re-quantizes its input to int8, so a rounding
+// difference anywhere upstream flips int8 codes, and flips grow through the
+// layers (a 1e-7 relative perturbation of the attention outputs alone moves the
+// 18-layer random-init model's last hidden state by ~2e-2).  Matching the
+// reference therefore means computing what it computes, in its order:
+//   score(j)  lane l (0..7) chains q[8r+l]*k[8r+l] over r with fused multiply-adds
+//             (NEXTERA_DOT64, :710-714); keys are grouped in 8s from the first
+//             key the query sees: a full group reduces ((a0+a1)+(a2+a3)) +
+//             ((a4+a5)+(a6+a7)), the n%8 keys after the last full group reduce
+//             as hsum256; then * scale (:704-730)
+//   softmax   m = max; full groups: e = exp256(s - m) (its Cephes polynomial),
+//             summed per lane in key order, then hsum256; the tail keys: e =
+//             exp(s - m) from the C library, added in order (:178-198); inv = 1/sum
+//   values    o[d] = fma(e_j * inv, v_j[d], o[d]) over the keys in order (:733-754)
+// The tail exp is computed in double precision and rounded to fp32 (correctly
+// rounded), which equals glibc's expf on all but 8.7e-5 of arguments (counted
+// over every float in [-90, 0]); every other operation is the same IEEE fp32
+// operation, so the output is bit-identical except where such a tail exp differs.
 //
-// Work item = (document, 64-query tile, KV head g).  The CTA holds 64 queries for
-// each of the H/G query heads that share g, so every K/V tile loaded into
-// shared memory serves all of them.  Thread = (query, head); q and the output
-// accumulator live in registers.  Items are planned on the host (key range per
-// tile: the whole document, or the band around the tile) and ordered longest
-// first.
+// Work item = (document, 32-query tile, KV head g).  The CTA holds the H/G query
+// heads that share g; two threads share one (query, head): thread `sub` keeps
+// lanes 4*sub .. 4*sub+3 of the 8-lane accumulators (q and the output dims
+// 8r + 4*sub + i).  Keys and values stream through shared memory in 32-key
+// tiles.  The softmax max must be known before any exp, so the pass over the
+// keys runs three times: max, then exp-sum, then the weighted sum of values
+// (scores are recomputed each time; O(T) memory for any document length).
 #include "common.cuh"
 #include "nextera_kernels.h"
 
@@ -26,7 +39,7 @@ namespace nxk {
 namespace attn {
 
 constexpr int D = 64;
-constexpr int QT = 64;      // queries per tile
+constexpr int QT = 32;      // queries per tile
 constexpr int KT = 32;      // keys per shared-memory tile
 
 struct Item {
@@ -35,112 +48,202 @@ struct Item {
     int doc;
 };
 
+// exp for the softmax tail: correctly rounded fp32 exp (see above)
+__device__ __forceinline__ float exp_tail(float x) { return (float) exp((double) x); }
+
+struct Lanes {
+    float a[4];      // this thread's 4 of the 8 lane accumulators
+};
+
+// the thread's 4 lanes of NEXTERA_DOT64 for one key row
+__device__ __forceinline__ void dot_lanes(const float (&q)[8][4], const float * krow, int sub, Lanes & r) {
+#pragma unroll
+    for (int r8 = 0; r8 < 8; ++r8) {
+        const float4 kk = *(const float4 *) (krow + 8 * r8 + 4 * sub);
+        if (r8 == 0) {
+            r.a[0] = __fmul_rn(q[0][0], kk.x);
+            r.a[1] = __fmul_rn(q[0][1], kk.y);
+            r.a[2] = __fmul_rn(q[0][2], kk.z);
+            r.a[3] = __fmul_rn(q[0][3], kk.w);
+        } else {
+            r.a[0] = __fmaf_rn(q[r8][0], kk.x, r.a[0]);
+            r.a[1] = __fmaf_rn(q[r8][1], kk.y, r.a[1]);
+            r.a[2] = __fmaf_rn(q[r8][2], kk.z, r.a[2]);
+            r.a[3] = __fmaf_rn(q[r8][3], kk.w, r.a[3]);
+        }
+    }
+}
+
+// score of one key for both threads of the pair; `full`: the key is in a whole
+// group of 8.  All 32 lanes of the warp must call this (shuffles).
+__device__ __forceinline__ float pair_score(const Lanes & r, int sub, bool full, float scale) {
+    // full group: each thread reduces its 4 lanes, the pair adds the halves
+    const float half = __fadd_rn(__fadd_rn(r.a[0], r.a[1]), __fadd_rn(r.a[2], r.a[3]));
+    const float other = __shfl_xor_sync(0xffffffffu, half, 1);
+    const float t_full = sub == 0 ? __fadd_rn(half, other) : __fadd_rn(other, half);
+    // tail key: hsum256 = ((a0+a4) + (a2+a6)) + ((a1+a5) + (a3+a7))
+    float p[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) p[i] = __shfl_xor_sync(0xffffffffu, r.a[i], 1);
+    float x[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[i] = __fadd_rn(r.a[i], p[i]);
+    const float t_tail = __fadd_rn(__fadd_rn(x[0], x[2]), __fadd_rn(x[1], x[3]));
+    return full ? __fmul_rn(t_full, scale) : __fmul_rn(scale, t_tail);
+}
+
 template <int REP>
-__global__ void __launch_bounds__(QT * REP)
+__global__ void __launch_bounds__(QT * REP * 2)
 attn_kernel(const float * __restrict__ q, const float * __restrict__ k, const float * __restrict__ v,
             float * __restrict__ out, const Item * __restrict__ items, const float * __restrict__ scale,
             const int32_t * __restrict__ doc_start, const int32_t * __restrict__ doc_len, int T, int H, int half) {
     __shared__ __align__(16) float Ks[KT][D];
     __shared__ __align__(16) float Vs[KT][D];
+    constexpr int NT = QT * REP * 2;
 
     const Item it = items[blockIdx.x];
     const int g = blockIdx.y;
-    const int hq = threadIdx.x / QT, qi = threadIdx.x % QT;
+    const int sub = threadIdx.x & 1, pair = threadIdx.x >> 1;
+    const int hq = pair / QT, qi = pair % QT;
     const int h = g * REP + hq;
     const int t = it.q0 + qi;
     const bool valid = t < it.q1;
-    const int lo_d = doc_start[it.doc], hi_d = lo_d + doc_len[it.doc];
-    int lo = lo_d, hi = hi_d;
+    const int dlo = doc_start[it.doc], dhi = dlo + doc_len[it.doc];
+    int lo = dlo, hi = dhi;
     if (half >= 0) {
         lo = max(lo, t - half);
         hi = min(hi, t + half + 1);
     }
-    const float sc = scale[it.doc] * 1.4426950408889634f;     // scores in log2 units
+    if (!valid) { lo = 0; hi = 0; }
+    const int n = hi - lo;
+    const int full_end = lo + (n & ~7);          // keys before this are in whole groups of 8
+    const float sc = scale[it.doc];
 
-    float qr[D];
-    if (valid) {
-        const float4 * qp = (const float4 *) (q + (size_t) t * H * D + (size_t) h * D);
+    float qv[8][4];
+    {
+        const float * qp = q + (size_t) (valid ? t : it.q0) * H * D + (size_t) h * D;
 #pragma unroll
-        for (int d4 = 0; d4 < D / 4; ++d4) {
-            const float4 x = qp[d4];
-            qr[4 * d4] = x.x; qr[4 * d4 + 1] = x.y; qr[4 * d4 + 2] = x.z; qr[4 * d4 + 3] = x.w;
+        for (int r8 = 0; r8 < 8; ++r8) {
+            const float4 x = *(const float4 *) (qp + 8 * r8 + 4 * sub);
+            qv[r8][0] = x.x; qv[r8][1] = x.y; qv[r8][2] = x.z; qv[r8][3] = x.w;
         }
-    } else {
-#pragma unroll
-        for (int d = 0; d < D; ++d) qr[d] = 0.0f;
     }
-    float o[D];
-#pragma unroll
-    for (int d = 0; d < D; ++d) o[d] = 0.0f;
-    float m = -INFINITY, l = 0.0f;
-
     const float * kg = k + (size_t) g * T * D;
     const float * vg = v + (size_t) g * T * D;
-    for (int kt = it.k0; kt < it.k1; kt += KT) {
-        const int nk = min(KT, it.k1 - kt);
-        // cooperative load of the key / value tile (float4, zero-filled past nk)
-        for (int i = threadIdx.x; i < KT * D / 4; i += QT * REP) {
+
+    auto load_tile = [&](int kt, int nk, bool with_v) {
+        for (int i = threadIdx.x; i < KT * D / 4; i += NT) {
             const int j = i / (D / 4), d4 = i % (D / 4);
             float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
             if (j < nk) {
                 kv = ((const float4 *) (kg + (size_t) (kt + j) * D))[d4];
-                vv = ((const float4 *) (vg + (size_t) (kt + j) * D))[d4];
+                if (with_v) vv = ((const float4 *) (vg + (size_t) (kt + j) * D))[d4];
             }
             ((float4 *) Ks[j])[d4] = kv;
-            ((float4 *) Vs[j])[d4] = vv;
+            if (with_v) ((float4 *) Vs[j])[d4] = vv;
+        }
+    };
+
+    // ---- pass 1: the maximum score (exact whatever the order)
+    float m = -INFINITY;
+    for (int kt = it.k0; kt < it.k1; kt += KT) {
+        const int nk = min(KT, it.k1 - kt);
+        load_tile(kt, nk, false);
+        __syncthreads();
+        for (int j = 0; j < nk; ++j) {
+            Lanes r;
+            dot_lanes(qv, Ks[j], sub, r);
+            const int kj = kt + j;
+            const float s = pair_score(r, sub, kj < full_end, sc);
+            if (kj >= lo && kj < hi) m = (m < s) ? s : m;
         }
         __syncthreads();
-        float s[KT];
-        float mt = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < KT; ++j) {
-            float acc = 0.0f;
-#pragma unroll
-            for (int d4 = 0; d4 < D / 4; ++d4) {
-                const float4 kk = ((const float4 *) Ks[j])[d4];
-                acc = fmaf(qr[4 * d4], kk.x, acc);
-                acc = fmaf(qr[4 * d4 + 1], kk.y, acc);
-                acc = fmaf(qr[4 * d4 + 2], kk.z, acc);
-                acc = fmaf(qr[4 * d4 + 3], kk.w, acc);
-            }
+    }
+
+    // ---- pass 2: e = exp256(s - m) over whole groups, summed per lane in key order
+    float vs[4] = {0.f, 0.f, 0.f, 0.f};       // lanes 4*sub .. 4*sub+3 of the 8 sum lanes
+    for (int kt = it.k0; kt < it.k1; kt += KT) {
+        const int nk = min(KT, it.k1 - kt);
+        load_tile(kt, nk, false);
+        __syncthreads();
+        for (int j = 0; j < nk; ++j) {
+            Lanes r;
+            dot_lanes(qv, Ks[j], sub, r);
             const int kj = kt + j;
-            s[j] = (j < nk && kj >= lo && kj < hi) ? acc * sc : -INFINITY;
-            mt = fmaxf(mt, s[j]);
-        }
-        const float mn = fmaxf(m, mt);
-        if (mn != -INFINITY) {
-            const float corr = exp2f(m - mn);          // m = -inf -> 0
-            l *= corr;
+            const float s = pair_score(r, sub, true, sc);
+            if (kj >= lo && kj < full_end) {
+                const float e = exp8(__fsub_rn(s, m));
+                const int l = (kj - lo) & 7;
 #pragma unroll
-            for (int d = 0; d < D; ++d) o[d] *= corr;
-#pragma unroll
-            for (int j = 0; j < KT; ++j) {
-                const float p = exp2f(s[j] - mn);     // masked -> 0
-                l += p;
-#pragma unroll
-                for (int d4 = 0; d4 < D / 4; ++d4) {
-                    const float4 vv = ((const float4 *) Vs[j])[d4];
-                    o[4 * d4]     = fmaf(p, vv.x, o[4 * d4]);
-                    o[4 * d4 + 1] = fmaf(p, vv.y, o[4 * d4 + 1]);
-                    o[4 * d4 + 2] = fmaf(p, vv.z, o[4 * d4 + 2]);
-                    o[4 * d4 + 3] = fmaf(p, vv.w, o[4 * d4 + 3]);
+                for (int i = 0; i < 4; ++i) {
+                    if (l == 4 * sub + i) vs[i] = __fadd_rn(vs[i], e);
                 }
             }
-            m = mn;
+        }
+        __syncthreads();
+    }
+    // hsum256 of the 8 lanes, then the tail keys in order with the C library's exp
+    float sum;
+    {
+        float p[4], x[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) p[i] = __shfl_xor_sync(0xffffffffu, vs[i], 1);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) x[i] = __fadd_rn(vs[i], p[i]);
+        sum = __fadd_rn(__fadd_rn(x[0], x[2]), __fadd_rn(x[1], x[3]));
+    }
+    for (int i = 0; i < 7; ++i) {                 // warp-uniform trip count: the shuffles need every lane
+        const int kj = full_end + i;
+        const bool act = kj < hi;
+        Lanes r;
+        dot_lanes(qv, kg + (size_t) (act ? kj : 0) * D, sub, r);
+        const float s = pair_score(r, sub, false, sc);
+        if (act) sum = __fadd_rn(sum, exp_tail(__fsub_rn(s, m)));
+    }
+    const float inv = __fdiv_rn(1.0f, sum);
+
+    // ---- pass 3: o[d] = fma(e_j * inv, v_j[d], o[d]) over the keys in order
+    float o[8][4];
+#pragma unroll
+    for (int r8 = 0; r8 < 8; ++r8) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[r8][i] = 0.0f;
+    }
+    for (int kt = it.k0; kt < it.k1; kt += KT) {
+        const int nk = min(KT, it.k1 - kt);
+        load_tile(kt, nk, true);
+        __syncthreads();
+        for (int j = 0; j < nk; ++j) {
+            Lanes r;
+            dot_lanes(qv, Ks[j], sub, r);
+            const int kj = kt + j;
+            const bool full = kj < full_end;
+            const float s = pair_score(r, sub, full, sc);
+            if (kj >= lo && kj < hi) {
+                const float x = __fsub_rn(s, m);
+                const float c = __fmul_rn(full ? exp8(x) : exp_tail(x), inv);
+#pragma unroll
+                for (int r8 = 0; r8 < 8; ++r8) {
+                    const float4 vv = *(const float4 *) (Vs[j] + 8 * r8 + 4 * sub);
+                    o[r8][0] = __fmaf_rn(c, vv.x, o[r8][0]);
+                    o[r8][1] = __fmaf_rn(c, vv.y, o[r8][1]);
+                    o[r8][2] = __fmaf_rn(c, vv.z, o[r8][2]);
+                    o[r8][3] = __fmaf_rn(c, vv.w, o[r8][3]);
+                }
+            }
         }
         __syncthreads();
     }
     if (valid) {
-        const float inv = 1.0f / l;
-        float4 * op = (float4 *) (out + (size_t) t * H * D + (size_t) h * D);
+        float * op = out + (size_t) t * H * D + (size_t) h * D;
 #pragma unroll
-        for (int d4 = 0; d4 < D / 4; ++d4) {
-            op[d4] = make_float4(o[4 * d4] * inv, o[4 * d4 + 1] * inv, o[4 * d4 + 2] * inv, o[4 * d4 + 3] * inv);
+        for (int r8 = 0; r8 < 8; ++r8) {
+            *(float4 *) (op + 8 * r8 + 4 * sub) = make_float4(o[r8][0], o[r8][1], o[r8][2], o[r8][3]);
         }
     }
 }
 
-// one 64-query tile per item; key range = document or band
+// one QT-query tile per item; key range = document, or the band around the tile
 void plan(const int32_t * start, const int32_t * len, int n_docs, int half, std::vector<Item> & items) {
     items.clear();
     for (int d = 0; d < n_docs; ++d) {
@@ -183,23 +286,22 @@ int nxk_attention(const float * q, const float * k, const float * v, int T, int 
                   size_t workspace_bytes, float * out, void * stream) {
     if (T < 0 || H <= 0 || G <= 0 || H % G || D != attn::D || n_docs < 0) return NXK_EINVAL;
     const int rep = H / G;
-    if (rep != 1 && rep != 2 && rep != 4) return NXK_EINVAL;     // thread count 64 * rep, registers bound rep <= 4
+    if (rep != 1 && rep != 2 && rep != 4) return NXK_EINVAL;     // 64 * rep threads per block
     if (T == 0 || n_docs == 0) return NXK_OK;
     std::vector<attn::Item> items;
     attn::plan(h_doc_start, h_doc_len, n_docs, half, items);
     const size_t bytes = items.size() * sizeof(attn::Item);
     if (!workspace || workspace_bytes < bytes) return NXK_EINVAL;
     cudaStream_t s = (cudaStream_t) stream;
+    // from pageable memory: staged by CUDA before the call returns, so `items` may go
     if (cudaMemcpyAsync(workspace, items.data(), bytes, cudaMemcpyHostToDevice, s) != cudaSuccess) return NXK_ELAUNCH;
     const dim3 grid((unsigned) items.size(), (unsigned) G);
     const attn::Item * it = (const attn::Item *) workspace;
     switch (rep) {
-        case 1: attn::attn_kernel<1><<<grid, attn::QT * 1, 0, s>>>(q, k, v, out, it, scale, doc_start, doc_len, T, H, half); break;
-        case 2: attn::attn_kernel<2><<<grid, attn::QT * 2, 0, s>>>(q, k, v, out, it, scale, doc_start, doc_len, T, H, half); break;
-        default: attn::attn_kernel<4><<<grid, attn::QT * 4, 0, s>>>(q, k, v, out, it, scale, doc_start, doc_len, T, H, half); break;
+        case 1: attn::attn_kernel<1><<<grid, attn::QT * 2, 0, s>>>(q, k, v, out, it, scale, doc_start, doc_len, T, H, half); break;
+        case 2: attn::attn_kernel<2><<<grid, attn::QT * 4, 0, s>>>(q, k, v, out, it, scale, doc_start, doc_len, T, H, half); break;
+        default: attn::attn_kernel<4><<<grid, attn::QT * 8, 0, s>>>(q, k, v, out, it, scale, doc_start, doc_len, T, H, half); break;
     }
-    // the host item list may be freed on return: the copy above is from pageable
-    // memory, which CUDA stages before cudaMemcpyAsync returns
     return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
 }
 

@@ -40,3 +40,11 @@ def tiny_model_path():
 def tiny_q8_path():
     import synth_model as sm
     return sm.cached_model("tiny", sm.tiny_hparams(), "Q8_0", seed=1)
+
+
+@pytest.fixture(autouse=True)
+def _release_device_copies():
+    yield
+    gl = sys.modules.get("gpulib")
+    if gl is not None and gl._KEEP:
+        gl.release()

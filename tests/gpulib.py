@@ -88,9 +88,23 @@ def load_lib(path=None):
 
 # -- torch plumbing -------------------------------------------------------------
 
+# Device copies made by dev() stay referenced here until the test ends
+# (tests/conftest.py releases them), so a raw pointer taken from a temporary
+# tensor is never recycled by torch's caching allocator while still in use.
+_KEEP: list = []
+
+
 def dev(a: np.ndarray):
     import torch
-    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    _KEEP.append(t)
+    return t
+
+
+def release():
+    import torch
+    torch.cuda.synchronize()
+    _KEEP.clear()
 
 
 def empty(shape, dtype):
@@ -143,6 +157,7 @@ class Ops:
         T, K = xq.shape
         N = w.shape[0]
         out = empty((T, N), torch.float32)
+        out.fill_(float("nan"))             # every output must be written
         fn = self.L.nxk_linear_i8_simt if simt else self.L.nxk_linear_i8
         self._ok(fn(P(dev(xq)), P(dev(sx)), T, P(dev(w)), P(dev(sw)), K, N, P(None if res is None else dev(res)),
                     P(out), stream_ptr()), "linear")

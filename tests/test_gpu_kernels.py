@@ -1,8 +1,10 @@
 """GPU kernels against the CPU oracle, one kernel at a time (needs a B200).
 
 Bar: bit-identical for everything integer and for every fp32 row op (they
-perform the reference's operations in the reference's order); attention within
-1e-4 of the output's largest magnitude (online softmax, different exp).
+perform the reference's operations in the reference's order).  Attention also
+follows the reference's order; its softmax tail exp is correctly rounded where
+the reference calls glibc's expf, so it must be within 1e-4 of the output's
+largest magnitude (the configuration's bar) and bit-identical almost everywhere.
 """
 import numpy as np
 import pytest
@@ -211,6 +213,9 @@ def test_attention_vs_oracle(ops, oracle, half):
     want = oracle.attention(q, k, v, 4, 2, 64, half, scale, cases.LENGTHS_ATTN)
     err = np.abs(got - want).max() / np.abs(want).max()
     assert err <= 1e-4, err
+    same = float(np.mean(got == want))
+    print(f"attention half={half}: max rel err {err:.2e}, bit-identical fraction {same:.6f}")
+    assert same >= 0.999
 
 
 @pytest.mark.parametrize("half", [64, -1])
@@ -234,6 +239,7 @@ def test_cfg2_attention(ops, oracle, half):
                                 np.array([n], np.int32))
         err = np.abs(got[s0:s0 + n] - want).max() / np.abs(want).max()
         assert err <= 1e-4, (d, err)
+        assert float(np.mean(got[s0:s0 + n] == want)) >= 0.999, d
 
 
 def test_layer_norm_and_pool(ops, oracle):

@@ -60,6 +60,7 @@ class Model:
 def compare(got, want, what):
     rel = float(np.linalg.norm(got - want) / np.linalg.norm(want))
     cos = np.sum(got * want, 1) / (np.linalg.norm(got, axis=1) * np.linalg.norm(want, axis=1))
+    print(f"{what}: rel err {rel:.3e}, min token cosine {cos.min():.8f}, bit-identical {np.mean(got == want):.6f}")
     assert rel <= REL_TOL, f"{what}: relative error {rel:.3e}"
     assert cos.min() >= COS_MIN, f"{what}: min token cosine {cos.min():.6f}"
     return rel, float(cos.min())
