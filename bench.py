@@ -1,0 +1,446 @@
+#!/usr/bin/env python
+"""Throughput benchmark: encoded tokens/s on the mixed-length batch (config 4).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl b200|reference] [--preset Q4_K_M]
+
+Workload (per GPU): 4096 documents with lengths log-uniform in [16, 2048]
+(seed = rank; 1,685,650 tokens at seed 0), token ids uniform over the vocabulary,
+through the random-init NexteraBERT model (18 layers, hidden 1024) quantized to
+Q4_K_M; pooled, L2-normalised embeddings out.  A step is one nextera_encode of
+the whole batch.  With N GPUs every rank encodes its own batch on its own model
+replica (sequence-partitioned data parallelism, no collective on the data path),
+so the global batch grows with N ("scaling": "weak").
+
+  value   tokens/s of all ranks, inputs already in HBM (nextera_encode_device),
+          K steps timed with CUDA events on the launching stream, barrier and
+          synchronize on both sides, max over ranks
+  e2e     the same metric through the public host API (nextera_encode): token ids
+          from pinned host memory in, pooled embeddings back to the host, per step
+  roofline, shares: per-kind device time from the library's profiler (one extra
+          untimed step), the dominant kind against the measured peak
+  cpu_baseline: the reference's own C++ (oracle/_ref, compiled from its sources)
+          on this host's cores over a bounded sample of the same batch (rank 0, N=1)
+
+--impl reference times only that CPU implementation (rank 0; other ranks exit).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "tests"))
+sys.path.insert(0, str(ROOT / "tests" / "golden"))
+
+METRIC = "encoded tokens/s (mixed-length batch, Q4_K_M)"
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ---------------------------------------------------------------- workload
+def workload(rank: int, n_docs: int):
+    import synth_model as sm
+    lengths = sm.throughput_lengths(n_docs, 16, 2048, seed=rank)
+    tokens = sm.random_tokens(int(lengths.sum()), 50368, seed=1000 + rank)
+    return tokens, lengths
+
+
+def model_path(preset: str, rank: int, world: int, dist):
+    import synth_model as sm
+    hp = sm.full_hparams()
+    if rank == 0:
+        p = sm.cached_model("full", hp, preset, seed=0)
+    if world > 1:
+        dist.barrier()
+    if rank != 0:
+        p = sm.cached_model("full", hp, preset, seed=0)
+    return p
+
+
+def linear_ops(lengths) -> float:
+    """Algorithmic int8 multiply-adds x 2 of one step (every linear layer, full model)."""
+    C, I, H, G, D, r = 1024, 2304, 16, 8, 64, 64
+    T = float(np.sum(lengths))
+    nb = float(np.sum((lengths + 3) // 4))
+    import synth_model as sm
+    macs = 0.0
+    for bt in sm.FULL_BLOCKS:
+        if bt == "lily":
+            macs += T * (2 * r * C + C * r + 3 * C * C)
+        elif bt in ("swa", "attn"):
+            macs += T * (H * D * C + 2 * G * D * C + C * H * D + C * C)
+        else:
+            macs += T * 5 * C * C + nb * (H * D * C + 2 * G * D * C)
+        macs += T * 2 * C * I
+    return 2.0 * macs
+
+
+def attention_work(lengths):
+    """(fp32 FLOPs of scores + weighted values, algorithmic bytes of q/k/v/out) of one step."""
+    H, G, D, half = 16, 8, 64, 128
+    import synth_model as sm
+    L = lengths.astype(np.float64)
+    nb = np.ceil(L / 4)
+    flops, bytes_ = 0.0, 0.0
+    for bt in sm.FULL_BLOCKS:
+        if bt == "lily":
+            continue
+        if bt == "swa":
+            # keys per query: min(L, t + half + 1) - max(0, t - half), summed over t
+            keys = 0.0
+            for n in lengths:
+                t = np.arange(n)
+                keys += float(np.sum(np.minimum(n, t + half + 1) - np.maximum(0, t - half)))
+            rows = float(L.sum())
+        elif bt == "attn":
+            keys, rows = float(np.sum(L * L)), float(L.sum())
+        else:
+            keys, rows = float(np.sum(nb * nb)), float(nb.sum())
+        flops += 4.0 * H * D * keys
+        bytes_ += 4.0 * rows * (2 * H * D + 2 * G * D)
+    return flops, bytes_
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", gpu_id, "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- CPU reference
+def reference_runner():
+    """(encode function, cores, kind): the reference compiled here, else the oracle port."""
+    from oracle_lib import Oracle, RefLib, ref_library_path
+    cores = os.cpu_count() or 1
+    if ref_library_path() is not None:
+        ref = RefLib()
+        state = {}
+
+        def run(path, tokens, lengths):
+            if "h" not in state:
+                state["h"] = ref.load(path, cores)
+            ref.encode(state["h"], tokens, lengths, hidden=False)
+        return run, cores, "reference"
+    o = Oracle()
+    o.L.or_set_threads(cores)
+    state = {}
+
+    def run(path, tokens, lengths):
+        if "m" not in state:
+            state["m"] = o.load(path)
+        state["m"].encode(tokens, lengths, hidden=False)
+    return run, cores, "port"
+
+
+def cpu_sample(run, path, tokens, lengths, target_s: float):
+    """Docs from the front of the batch whose encode takes about target_s seconds."""
+    start = np.concatenate([[0], np.cumsum(lengths)])
+    n = 8
+    run(path, tokens[:start[n]], lengths[:n])           # load + warm
+    t0 = time.perf_counter()
+    run(path, tokens[:start[n]], lengths[:n])
+    dt = max(time.perf_counter() - t0, 1e-3)
+    per_tok = dt / float(start[n])
+    want = int(target_s / per_tok)
+    n = int(np.searchsorted(start, want))
+    n = max(8, min(n, len(lengths)))
+    return tokens[:start[n]], lengths[:n]
+
+
+def time_cpu(run, path, tokens, lengths, steps: int, warmup: int):
+    for _ in range(warmup):
+        run(path, tokens, lengths)
+    ts = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        run(path, tokens, lengths)
+        ts.append(time.perf_counter() - t0)
+    return float(np.sum(lengths)) / (sum(ts) / len(ts)), 1000.0 * sum(ts) / len(ts)
+
+
+def base_line(args, world):
+    return {"metric": METRIC, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8+fp32",
+            "data": "synthetic (seeded lengths and token ids; random-init weights N(0,0.02), Q4_K_M)"}
+
+
+def config(args, world, tokens_per_gpu):
+    return {"workload": f"cfg4 mixed-length batch: {args.docs} docs/GPU, lengths log-uniform [16, 2048], "
+                        f"{args.preset} random-init NexteraBERT (18 layers, hidden 1024)",
+            "model": "NexteraBERT-synthetic (8 lily / 6 swa / 2 attn / 2 hra)", "preset": args.preset,
+            "docs_per_gpu": args.docs, "tokens_per_gpu_step": int(tokens_per_gpu),
+            "global_batch": args.docs * world, "seq_len": "16-2048 (unpadded)",
+            "parallelism": f"dp{world} (sequence-partitioned replicas)",
+            "l2": "inputs larger than L2 (each activation tensor ~6.9 GB)"}
+
+
+# ---------------------------------------------------------------- main
+def run_reference(args, rank, world, dist):
+    if rank != 0:
+        return
+    path = model_path(args.preset, 0, 1, None)
+    tokens, lengths = workload(0, args.docs)
+    run, cores, kind = reference_runner()
+    st, sl = cpu_sample(run, path, tokens, lengths, target_s=8.0)
+    v, ms = time_cpu(run, path, st, sl, args.steps, args.warmup)
+    sample = f"first {len(sl)} docs ({int(sl.sum())} tokens) of the rank-0 batch per step"
+    line = base_line(args, world)
+    line.update({"impl": "reference", "value": v, "ms_per_step": ms, "n_gpus": world,
+                 "config": config(args, world, int(lengths.sum())),
+                 "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": kind, "sample": sample},
+                 "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+    print(json.dumps(line), flush=True)
+
+
+def int8_peak_tops(torch) -> float:
+    """Measured dense int8 throughput of the library GEMM (cuBLASLt via torch._int_mm), TOPS."""
+    n = 8192
+    a = torch.randint(-127, 127, (n, n), dtype=torch.int8, device="cuda")
+    b = torch.randint(-127, 127, (n, n), dtype=torch.int8, device="cuda").t()
+    for _ in range(3):
+        torch._int_mm(a, b)
+    best = 1e30
+    for _ in range(10):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        torch._int_mm(a, b)
+        e.record()
+        e.synchronize()
+        best = min(best, s.elapsed_time(e))
+    del a, b
+    return 2.0 * n ** 3 / (best * 1e-3) / 1e12
+
+
+def run_b200(args, rank, world, local_rank, dist):
+    import torch
+    from gpulib import load_lib
+
+    torch.cuda.set_device(local_rank)
+    dev_uuid = str(torch.cuda.get_device_properties(local_rank).uuid)
+    gpu_id = dev_uuid if dev_uuid.startswith("GPU-") else f"GPU-{dev_uuid}"
+    L = load_lib()
+    path = model_path(args.preset, rank, world, dist)
+    tokens, lengths = workload(rank, args.docs)
+    T, n_docs, C = int(lengths.sum()), len(lengths), 1024
+    h = L.nextera_load(str(path).encode(), L.nextera_default_params())
+    assert h, "nextera_load failed"
+    stream = torch.cuda.current_stream()
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+    d_tok = torch.from_numpy(tokens).cuda()
+    d_pool = torch.empty((n_docs, C), dtype=torch.float32, device="cuda")
+    lens = np.ascontiguousarray(lengths, np.int32)
+    i32 = ctypes.POINTER(ctypes.c_int32)
+    lens_p = lens.ctypes.data_as(i32)
+
+    def step():
+        rc = L.nextera_encode_device(h, ctypes.c_void_p(d_tok.data_ptr()), None, lens_p, n_docs, None,
+                                     ctypes.c_void_p(d_pool.data_ptr()), 1, sptr)
+        assert rc == 0, f"nextera_encode_device returned {rc}"
+
+    if args.profile_run:
+        step()
+        torch.cuda.synchronize()
+        return
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(gpu_id)
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    l0 = L.nextera_debug_launches(h)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    launches = int(L.nextera_debug_launches(h) - l0)
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        tt = torch.tensor([T], dtype=torch.float64, device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.SUM)
+        total_tokens = float(tt.item())
+    else:
+        total_tokens = float(T)
+    ms_step = ms / args.steps
+    value = total_tokens / (ms_step * 1e-3)
+
+    # e2e through the host API: pinned token ids in, pooled embeddings out
+    pinned = torch.from_numpy(tokens).pin_memory()
+    h_tok = pinned.numpy()
+    h_pool = torch.empty((n_docs, C), dtype=torch.float32).pin_memory().numpy()
+    f32 = ctypes.POINTER(ctypes.c_float)
+    rc = L.nextera_encode(h, h_tok.ctypes.data_as(i32), lens_p, n_docs, None, h_pool.ctypes.data_as(f32), 1)
+    assert rc == 0
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        rc = L.nextera_encode(h, h_tok.ctypes.data_as(i32), lens_p, n_docs, None, h_pool.ctypes.data_as(f32), 1)
+        assert rc == 0
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = {"value": total_tokens / e2e_s, "unit": "tokens/s",
+           "h2d_bytes_per_step": int(4 * T + 4 * (3 * T + (T + 3) // 4 + 4 * n_docs)),
+           "d2h_bytes_per_step": int(4 * n_docs * C), "ms_per_step": 1000.0 * e2e_s,
+           "api": "nextera_encode (host buffers)"}
+
+    # per-kind device time (one extra, untimed, profiled step)
+    L.nextera_debug_profile(h, 1)
+    rc = L.nextera_encode(h, h_tok.ctypes.data_as(i32), lens_p, n_docs, None, h_pool.ctypes.data_as(f32), 1)
+    kind = (ctypes.c_double * 3)()
+    tot = ctypes.c_double()
+    L.nextera_debug_profile_get(h, kind, ctypes.byref(tot))
+    L.nextera_debug_profile(h, 0)
+    k_ms = {"int8_linear": kind[0], "attention": kind[1], "row_ops": kind[2]}
+    dev_ms = sum(k_ms.values())
+    shares = {k: v / dev_ms for k, v in k_ms.items()}
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        pass
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    lin_ops = linear_ops(lengths)
+    att_flops, att_bytes = attention_work(lengths)
+    top = max(k_ms, key=k_ms.get)
+    roof = None
+    if rank == 0:
+        i8_peak = int8_peak_tops(torch)
+        lin = {"bound": "tensor", "achieved": lin_ops / (k_ms["int8_linear"] * 1e-3) / 1e12, "peak": i8_peak,
+               "unit": "TOPS", "kernel": "gemm_i8_tc (int8 linear layers)",
+               "peak_source": "dense int8 GEMM measured in this run (cuBLASLt via torch._int_mm, 8192^3, burst)",
+               "algorithmic": "sum over the step's 141-per-token int8 linears of 2*T*N*K"}
+        lin["frac"] = lin["achieved"] / lin["peak"]
+        att = {"bound": "hbm", "achieved": att_bytes / (k_ms["attention"] * 1e-3) / 1e9, "peak": hbm_peak,
+               "unit": "GB/s", "kernel": "attn_kernel (exact varlen GQA)",
+               "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)",
+               "algorithmic": "q + k + v read, output written once per attention layer (fp32)",
+               "fp32_tflops": att_flops / (k_ms["attention"] * 1e-3) / 1e12}
+        att["frac"] = att["achieved"] / att["peak"]
+        roof = lin if top == "int8_linear" else att if top == "attention" else None
+        if roof is None:
+            roof = {"bound": "hbm", "achieved": None, "peak": hbm_peak, "unit": "GB/s", "frac": None,
+                    "kernel": "row ops"}
+        tf = ROOT / "profiles" / "traffic.json"
+        roof["traffic"] = None
+        if tf.exists():
+            try:
+                tr = json.loads(tf.read_text())
+                roof["traffic"] = tr.get(roof["kernel"].split()[0])
+            except ValueError:
+                pass
+        roof = dict(roof)
+        roof["by_kind"] = {"int8_linear": dict(lin), "attention": dict(att)}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        run, cores, kindname = reference_runner()
+        st, sl = cpu_sample(run, path, tokens, lengths, target_s=6.0)
+        cv, cms = time_cpu(run, path, st, sl, 1, 0)
+        cpu = {"value": cv, "unit": "tokens/s", "cores": cores, "kind": kindname,
+               "sample": f"first {len(sl)} docs ({int(sl.sum())} tokens) of the batch, one timed encode"}
+    L.nextera_free(h)
+    log(f"rank {rank}: {ms_step:.1f} ms/step, {value:.0f} tokens/s, e2e {e2e['value']:.0f} tokens/s, kinds {k_ms}")
+    if rank == 0:
+        line = base_line(args, world)
+        line.update({"value": value, "ms_per_step": ms_step, "config": config(args, world, T),
+                     "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
+                     "gpu_launches": launches, "device_ms_by_kind": k_ms, "shares": shares})
+        print(json.dumps(line), flush=True)
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--preset", default="Q4_K_M")
+    ap.add_argument("--docs", type=int, default=4096)
+    ap.add_argument("--profile-run", action="store_true", help="one untimed step (for profilers)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if args.impl == "reference":
+        run_reference(args, rank, world, dist)
+        return 0
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    try:
+        run_b200(args, rank, world, local_rank, dist)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

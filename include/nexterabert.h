@@ -119,6 +119,12 @@ NEXTERA_API double nextera_last_ms(const struct nextera_context * ctx);
 NEXTERA_API void nextera_debug_set_layers(struct nextera_context * ctx, int32_t n_layers);
 NEXTERA_API void nextera_debug_profile(struct nextera_context * ctx, int32_t enable);
 NEXTERA_API void nextera_debug_profile_print(const struct nextera_context * ctx);
+/* Number of device kernels this context has launched since nextera_load (no
+ * counterpart in the reference; lets a benchmark count the launches it timed). */
+NEXTERA_API int64_t nextera_debug_launches(const struct nextera_context * ctx);
+/* The profile's totals as numbers: kind_ms[3] = device ms in int8 linear / attention /
+ * row ops, *total_ms = wall ms of the profiled calls; returns the number of calls. */
+NEXTERA_API int64_t nextera_debug_profile_get(const struct nextera_context * ctx, double * kind_ms, double * total_ms);
 
 /* Device-resident variant of nextera_encode_segments: tokens / token_types are
  * device pointers, hidden / pooled device pointers (either may be NULL), lengths

@@ -128,6 +128,7 @@ struct nextera_context {
     int32_t debug_n_layers = -1;
     profiler prof;
     double last_ms = 0.0;
+    int64_t launches = 0;          // kernels launched since load (all calls)
 
     bool has(const std::string & n) const {
         return i8.count(n) || f32.count(n) || taps.count(n) || raw.count(n) ||
@@ -504,6 +505,14 @@ void nextera_set_n_threads(struct nextera_context * c, int32_t n) {
 
 void nextera_debug_set_layers(struct nextera_context * c, int32_t n_layers) { c->debug_n_layers = n_layers; }
 
+int64_t nextera_debug_launches(const struct nextera_context * c) { return c->launches; }
+
+int64_t nextera_debug_profile_get(const struct nextera_context * c, double * kind_ms, double * total_ms) {
+    for (int i = 0; i < PROF_COUNT; ++i) kind_ms[i] = c->prof.ms[i];
+    *total_ms = c->prof.total_ms;
+    return c->prof.calls;
+}
+
 void nextera_debug_profile(struct nextera_context * c, int32_t enable) {
     for (auto & m : c->prof.marks) cudaEventDestroy(m.first);
     c->prof = profiler();
@@ -564,6 +573,7 @@ public:
             return;
         }
         mark(PROF_LINEAR);
+        ++c_.launches;
         const I8Weight & w = it->second;
         ok = check(nxk_linear_i8(q, sx, T, w.w.as<int8_t>(), w.scale.as<float>(), w.n_in, w.n_out, res, out, s_),
                    name.c_str());
@@ -594,7 +604,9 @@ public:
         return &it->second;
     }
 
-    void rows(int rc, const char * what) {
+    // a row-op / attention / embedding launch (pooling launches two kernels)
+    void rows(int rc, const char * what, int n_kernels = 1) {
+        c_.launches += n_kernels;
         if (ok) ok = check(rc, what);
     }
 
@@ -905,7 +917,7 @@ int run_encoder(nextera_context & c, const Batch & b, float rope0_base, const in
     }
     float * pooled = d_pooled_out ? d_pooled_out : c.pooled.as<float>();
     fw.mark(PROF_ROWS);
-    fw.rows(nxk_pool(hidden, L.start, L.len, b.n_docs, C, normalize, pooled, s), "pool");
+    fw.rows(nxk_pool(hidden, L.start, L.len, b.n_docs, C, normalize, pooled, s), "pool", 2);
     if (d_hidden_out) cudaMemcpyAsync(d_hidden_out, hidden, sizeof(float) * (size_t) T * C, cudaMemcpyDeviceToDevice, s);
     fw.mark(-1);
     if (!fw.ok) return 3;

@@ -79,6 +79,9 @@ def load_lib(path=None):
         "nextera_debug_set_layers": ([vp, ctypes.c_int32], None),
         "nextera_debug_profile": ([vp, ctypes.c_int32], None),
         "nextera_debug_profile_print": ([vp], None),
+        "nextera_debug_launches": ([vp], ctypes.c_int64),
+        "nextera_debug_profile_get": ([vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)],
+                                      ctypes.c_int64),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
