@@ -109,6 +109,22 @@ NEXTERA_API int nxk_attention(const float * q, const float * k, const float * v,
                               const int32_t * h_doc_start, const int32_t * h_doc_len,
                               void * workspace, size_t workspace_bytes, float * out, void * stream);
 
+/* nxk_attention without a workspace argument, for callers that cannot allocate
+ * device memory when they call (a host that hands this library pointers into a
+ * pool it manages itself and forbids cudaMalloc after start-up, or a path where a
+ * blocking allocation is not allowed).  No counterpart in the reference, whose
+ * CPU attention needs no device memory.  Its work plan lives in a fixed array
+ * inside the library (2.5 MiB on each device that loads it, kept until exit):
+ * at most 131072 query tiles per call, i.e. sum over documents of
+ * ceil(len / 32) <= 131072; larger batches return NXK_EINVAL.  h_doc_len is the
+ * host copy of doc_len.  The array's device address is looked up on the first
+ * call made with each device current, so make that first call before any stream
+ * capture.  Calls share the array: two calls in flight at the same time race. */
+NEXTERA_API int nxk_attention_noalloc(const float * q, const float * k, const float * v, int T, int H, int G, int D,
+                                      int half, const float * scale, const int32_t * doc_start,
+                                      const int32_t * doc_len, int n_docs, const int32_t * h_doc_len, float * out,
+                                      void * stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -306,3 +306,130 @@ int nxk_attention(const float * q, const float * k, const float * v, int T, int 
 }
 
 } // extern "C"
+
+// ---------------------------------------------------------------------------
+// nxk_attention_noalloc: the same attention without a caller-provided workspace.
+//
+// For callers that cannot allocate device memory at the point of the call: a
+// host that hands this library pointers into a pool it manages itself (a
+// serving framework's arena, a memory-mapped buffer shared with another
+// process) and forbids cudaMalloc after start-up, or code that must not touch
+// the allocator at all (a real-time path where cudaMalloc may block on the
+// device).  nxk_attention needs a workspace for its work plan; this variant
+// keeps the plan in a fixed array compiled into the library instead.
+//
+// The plan lives in g_noalloc_items, a file-scope __device__ array of
+// NOALLOC_MAX_ITEMS items (20 bytes each, 2.5 MiB on every device that loads
+// the library, held until exit).  One item is one 32-query tile of one
+// document, so a batch may hold at most NOALLOC_MAX_ITEMS tiles (sum over the
+// documents of ceil(len / 32)); larger batches are rejected with NXK_EINVAL and
+// a message.  The plan is written on the device by a small planner kernel from
+// doc_start / doc_len, in document order; every entry the attention kernel
+// reads is written by the same call first, so nothing needs clearing.  All calls
+// share the array: two calls whose work overlaps on the GPU (different streams,
+// no ordering between them) race on it and must not be issued.
+//
+// Host code cannot use the array's name as a device address; its address is
+// looked up once per device with cudaGetSymbolAddress on the first call made
+// with that device current.  That first call should therefore come before any
+// CUDA stream capture.  No device memory is allocated, and no host memory
+// either.
+// ---------------------------------------------------------------------------
+#include <cstdio>
+#include <mutex>
+
+namespace nxk {
+namespace attn {
+
+constexpr int NOALLOC_MAX_ITEMS = 1 << 17;
+constexpr int NOALLOC_MAX_DEVICES = 64;
+
+static __device__ __align__(256) Item g_noalloc_items[NOALLOC_MAX_ITEMS];
+
+// One block: each thread owns a contiguous run of documents, counts their tiles,
+// the block scans the counts, then every thread writes its documents' items.
+__global__ void __launch_bounds__(1024) plan_kernel(Item * __restrict__ items, const int32_t * __restrict__ doc_start,
+                                                    const int32_t * __restrict__ doc_len, int n_docs, int half) {
+    __shared__ int part[1024];
+    const int tid = threadIdx.x, nt = blockDim.x;
+    const int per = (n_docs + nt - 1) / nt;
+    const int d0 = min(n_docs, tid * per), d1 = min(n_docs, d0 + per);
+    int cnt = 0;
+    for (int d = d0; d < d1; ++d) cnt += (doc_len[d] + QT - 1) / QT;
+    part[tid] = cnt;
+    __syncthreads();
+    for (int off = 1; off < nt; off <<= 1) {        // inclusive scan (Hillis-Steele)
+        const int add = tid >= off ? part[tid - off] : 0;
+        __syncthreads();
+        part[tid] += add;
+        __syncthreads();
+    }
+    int o = part[tid] - cnt;
+    for (int d = d0; d < d1; ++d) {
+        const int lo = doc_start[d], hi = lo + doc_len[d];
+        for (int q0 = lo; q0 < hi; q0 += QT) {
+            Item it;
+            it.q0 = q0;
+            it.q1 = min(hi, q0 + QT);
+            it.doc = d;
+            it.k0 = half < 0 ? lo : max(lo, q0 - half);
+            it.k1 = half < 0 ? hi : min(hi, it.q1 - 1 + half + 1);
+            items[o++] = it;
+        }
+    }
+}
+
+// address of g_noalloc_items on the current device (looked up once per device)
+Item * noalloc_items() {
+    static std::mutex mu;
+    static Item * ptr[NOALLOC_MAX_DEVICES] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= NOALLOC_MAX_DEVICES) return nullptr;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!ptr[dev]) {
+        void * p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_items) != cudaSuccess) {
+            fprintf(stderr, "nxk_attention_noalloc: cudaGetSymbolAddress failed on device %d: %s\n", dev,
+                    cudaGetErrorString(cudaGetLastError()));
+            return nullptr;
+        }
+        ptr[dev] = (Item *) p;
+    }
+    return ptr[dev];
+}
+
+} // namespace attn
+} // namespace nxk
+
+extern "C" int nxk_attention_noalloc(const float * q, const float * k, const float * v, int T, int H, int G, int D,
+                                     int half, const float * scale, const int32_t * doc_start,
+                                     const int32_t * doc_len, int n_docs, const int32_t * h_doc_len, float * out,
+                                     void * stream) {
+    using namespace nxk::attn;
+    if (T < 0 || H <= 0 || G <= 0 || H % G || D != nxk::attn::D || n_docs < 0 || !h_doc_len) return NXK_EINVAL;
+    const int rep = H / G;
+    if (rep != 1 && rep != 2 && rep != 4) return NXK_EINVAL;
+    if (T == 0 || n_docs == 0) return NXK_OK;
+    long long n_items = 0;
+    for (int d = 0; d < n_docs; ++d) {
+        if (h_doc_len[d] <= 0) return NXK_EINVAL;
+        n_items += (h_doc_len[d] + QT - 1) / QT;
+    }
+    if (n_items > NOALLOC_MAX_ITEMS) {
+        fprintf(stderr, "nxk_attention_noalloc: %lld query tiles exceed the fixed plan of %d "
+                        "(at most %d tiles of %d queries per call)\n", n_items, NOALLOC_MAX_ITEMS,
+                NOALLOC_MAX_ITEMS, QT);
+        return NXK_EINVAL;
+    }
+    Item * items = noalloc_items();
+    if (!items) return NXK_ELAUNCH;
+    cudaStream_t s = (cudaStream_t) stream;
+    plan_kernel<<<1, 1024, 0, s>>>(items, doc_start, doc_len, n_docs, half);
+    const dim3 grid((unsigned) n_items, (unsigned) G);
+    switch (rep) {
+        case 1: attn_kernel<1><<<grid, QT * 2, 0, s>>>(q, k, v, out, items, scale, doc_start, doc_len, T, H, half); break;
+        case 2: attn_kernel<2><<<grid, QT * 4, 0, s>>>(q, k, v, out, items, scale, doc_start, doc_len, T, H, half); break;
+        default: attn_kernel<4><<<grid, QT * 8, 0, s>>>(q, k, v, out, items, scale, doc_start, doc_len, T, H, half); break;
+    }
+    return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
+}
