@@ -243,13 +243,161 @@ attn_kernel(const float * __restrict__ q, const float * __restrict__ k, const fl
     }
 }
 
-// one QT-query tile per item; key range = document, or the band around the tile
-void plan(const int32_t * start, const int32_t * len, int n_docs, int half, std::vector<Item> & items) {
+// ---------------------------------------------------------------------------
+// Stored-score kernel (used by nxk_attention).  Same arithmetic as attn_kernel;
+// the difference is where the scores live.  One thread owns one (query, head) and
+// all 64 lanes of its dot products (q in registers, keys broadcast from shared
+// memory), computes every score once, and keeps it in a per-CTA scratch slot in
+// global memory (sized for the longest key range of the launch; L2-resident for
+// the band layers).  Pass 2 walks the thread's own scores in groups of 8 for the
+// exp-sum; pass 3 re-derives each weight from the stored score and accumulates
+// the values.  Work units (tile, KV head) are spread over a persistent grid,
+// longest first.
+// ---------------------------------------------------------------------------
+constexpr int QT3 = 64;            // queries per work unit
+
+template <int REP>
+__global__ void __launch_bounds__(QT3 * REP)
+attn_scored_kernel(const float * __restrict__ q, const float * __restrict__ k, const float * __restrict__ v,
+                   float * __restrict__ out, const Item * __restrict__ items, int n_units, int G,
+                   const float * __restrict__ scale, const int32_t * __restrict__ doc_start,
+                   const int32_t * __restrict__ doc_len, int T, int H, int half, float * __restrict__ scratch,
+                   int slot_keys) {
+    constexpr int NT = QT3 * REP;
+    __shared__ __align__(16) float Ks[KT][D];
+    __shared__ __align__(16) float Vs[KT][D];
+    float * sc_base = scratch + (size_t) blockIdx.x * slot_keys * NT;   // [key - k0][thread]
+
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+        const Item it = items[u / G];
+        const int g = u % G;
+        const int hq = threadIdx.x / QT3, qi = threadIdx.x % QT3;
+        const int h = g * REP + hq;
+        const int t = it.q0 + qi;
+        const bool valid = t < it.q1;
+        int lo = doc_start[it.doc], hi = lo + doc_len[it.doc];
+        if (half >= 0) {
+            lo = max(lo, t - half);
+            hi = min(hi, t + half + 1);
+        }
+        if (!valid) { lo = it.k0; hi = it.k0; }
+        const int n = hi - lo;
+        const int full_end = lo + (n & ~7);
+        const float sc = scale[it.doc];
+        const float * kg = k + (size_t) g * T * D;
+        const float * vg = v + (size_t) g * T * D;
+
+        // ---- pass 1: every score once (stored), and their maximum
+        float m = -INFINITY;
+        {
+            float qr[D];
+            const float * qp = q + (size_t) (valid ? t : it.q0) * H * D + (size_t) h * D;
+#pragma unroll
+            for (int d4 = 0; d4 < D / 4; ++d4) {
+                const float4 x = *(const float4 *) (qp + 4 * d4);
+                qr[4 * d4] = x.x; qr[4 * d4 + 1] = x.y; qr[4 * d4 + 2] = x.z; qr[4 * d4 + 3] = x.w;
+            }
+            for (int kt = it.k0; kt < it.k1; kt += KT) {
+                const int nk = min(KT, it.k1 - kt);
+                for (int i = threadIdx.x; i < KT * D / 4; i += NT) {
+                    const int j = i / (D / 4), d4 = i % (D / 4);
+                    ((float4 *) Ks[j])[d4] = j < nk ? ((const float4 *) (kg + (size_t) (kt + j) * D))[d4]
+                                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+                __syncthreads();
+                for (int j = 0; j < nk; ++j) {
+                    float a[8];
+#pragma unroll
+                    for (int r8 = 0; r8 < 8; ++r8) {
+                        const float4 k0 = ((const float4 *) Ks[j])[2 * r8];
+                        const float4 k1 = ((const float4 *) Ks[j])[2 * r8 + 1];
+                        const float kk[8] = { k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w };
+#pragma unroll
+                        for (int l = 0; l < 8; ++l) {
+                            a[l] = r8 == 0 ? __fmul_rn(qr[l], kk[l]) : __fmaf_rn(qr[8 * r8 + l], kk[l], a[l]);
+                        }
+                    }
+                    const int kj = kt + j;
+                    float s;
+                    if (kj < full_end) {
+                        const float tt = __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3])),
+                                                   __fadd_rn(__fadd_rn(a[4], a[5]), __fadd_rn(a[6], a[7])));
+                        s = __fmul_rn(tt, sc);
+                    } else {
+                        const float tt = __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[4]), __fadd_rn(a[2], a[6])),
+                                                   __fadd_rn(__fadd_rn(a[1], a[5]), __fadd_rn(a[3], a[7])));
+                        s = __fmul_rn(sc, tt);
+                    }
+                    if (kj >= lo && kj < hi) {
+                        m = (m < s) ? s : m;
+                        sc_base[(size_t) (kj - it.k0) * NT + threadIdx.x] = s;
+                    }
+                }
+                __syncthreads();
+            }
+        }
+
+        // ---- pass 2: exp256 over whole groups of 8, summed per lane in key order; then the tail
+        float sum;
+        {
+            float vs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            const float * sp = sc_base + (size_t) (lo - it.k0) * NT + threadIdx.x;
+            for (int j = 0; j < (n & ~7); j += 8) {
+#pragma unroll
+                for (int l = 0; l < 8; ++l) vs[l] = __fadd_rn(vs[l], exp8(__fsub_rn(sp[(size_t) (j + l) * NT], m)));
+            }
+            sum = __fadd_rn(__fadd_rn(__fadd_rn(vs[0], vs[4]), __fadd_rn(vs[2], vs[6])),
+                            __fadd_rn(__fadd_rn(vs[1], vs[5]), __fadd_rn(vs[3], vs[7])));
+            for (int j = n & ~7; j < n; ++j) sum = __fadd_rn(sum, exp_tail(__fsub_rn(sp[(size_t) j * NT], m)));
+        }
+        const float inv = __fdiv_rn(1.0f, sum);
+
+        // ---- pass 3: o[d] = fma(e_j * inv, v_j[d], o[d]) over the keys in order
+        float o[D];
+#pragma unroll
+        for (int d = 0; d < D; ++d) o[d] = 0.0f;
+        for (int kt = it.k0; kt < it.k1; kt += KT) {
+            const int nk = min(KT, it.k1 - kt);
+            for (int i = threadIdx.x; i < KT * D / 4; i += NT) {
+                const int j = i / (D / 4), d4 = i % (D / 4);
+                ((float4 *) Vs[j])[d4] = j < nk ? ((const float4 *) (vg + (size_t) (kt + j) * D))[d4]
+                                                : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            __syncthreads();
+            for (int j = 0; j < nk; ++j) {
+                const int kj = kt + j;
+                if (kj >= lo && kj < hi) {
+                    const float x = __fsub_rn(sc_base[(size_t) (kj - it.k0) * NT + threadIdx.x], m);
+                    const float c = __fmul_rn(kj < full_end ? exp8(x) : exp_tail(x), inv);
+#pragma unroll
+                    for (int d4 = 0; d4 < D / 4; ++d4) {
+                        const float4 vv = ((const float4 *) Vs[j])[d4];
+                        o[4 * d4]     = __fmaf_rn(c, vv.x, o[4 * d4]);
+                        o[4 * d4 + 1] = __fmaf_rn(c, vv.y, o[4 * d4 + 1]);
+                        o[4 * d4 + 2] = __fmaf_rn(c, vv.z, o[4 * d4 + 2]);
+                        o[4 * d4 + 3] = __fmaf_rn(c, vv.w, o[4 * d4 + 3]);
+                    }
+                }
+            }
+            __syncthreads();
+        }
+        if (valid) {
+            float4 * op = (float4 *) (out + (size_t) t * H * D + (size_t) h * D);
+#pragma unroll
+            for (int d4 = 0; d4 < D / 4; ++d4) {
+                op[d4] = make_float4(o[4 * d4], o[4 * d4 + 1], o[4 * d4 + 2], o[4 * d4 + 3]);
+            }
+        }
+    }
+}
+
+// one qt-query tile per item; key range = document, or the band around the tile
+void plan(const int32_t * start, const int32_t * len, int n_docs, int half, int qt, std::vector<Item> & items) {
     items.clear();
     for (int d = 0; d < n_docs; ++d) {
         const int lo = start[d], hi = lo + len[d];
-        for (int q0 = lo; q0 < hi; q0 += QT) {
-            const int q1 = std::min(hi, q0 + QT);
+        for (int q0 = lo; q0 < hi; q0 += qt) {
+            const int q1 = std::min(hi, q0 + qt);
             Item it;
             it.q0 = q0;
             it.q1 = q1;
@@ -263,10 +411,39 @@ void plan(const int32_t * start, const int32_t * len, int n_docs, int half, std:
                      [](const Item & a, const Item & b) { return (a.k1 - a.k0) > (b.k1 - b.k0); });
 }
 
-size_t n_items(const int32_t * len, int n_docs) {
+size_t n_items(const int32_t * len, int n_docs, int qt) {
     size_t n = 0;
-    for (int d = 0; d < n_docs; ++d) n += (size_t) (len[d] + QT - 1) / QT;
+    for (int d = 0; d < n_docs; ++d) n += (size_t) (len[d] + qt - 1) / qt;
     return n;
+}
+
+// Score scratch of the stored-score kernel: one slot per resident CTA, each
+// holding (longest key range) x (threads) floats; threads sized for 4 heads per
+// KV head (the most this build runs).  Slots: 4 per SM, at least one per SM,
+// and no more than fit in 8 GiB.
+constexpr int SLOTS_PER_SM = 4;
+constexpr size_t SCRATCH_BUDGET = (size_t) 8 << 30;
+
+struct Scratch {
+    int slot_keys = 0;
+    int slots = 0;
+    size_t bytes = 0;
+};
+
+Scratch scratch_plan(const int32_t * len, int n_docs, int half) {
+    int max_len = 0;
+    for (int d = 0; d < n_docs; ++d) max_len = std::max(max_len, (int) len[d]);
+    Scratch sp;
+    sp.slot_keys = half < 0 ? max_len : std::min(max_len, QT3 + 2 * half);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+    const size_t slot_bytes = (size_t) sp.slot_keys * QT3 * 4 * sizeof(float);
+    size_t slots = (size_t) sms * SLOTS_PER_SM;
+    if (slot_bytes > 0 && slots * slot_bytes > SCRATCH_BUDGET) slots = std::max((size_t) sms, SCRATCH_BUDGET / slot_bytes);
+    sp.slots = (int) slots;
+    sp.bytes = slots * slot_bytes;
+    return sp;
 }
 
 } // namespace attn
@@ -276,8 +453,9 @@ using namespace nxk;
 
 extern "C" {
 
-size_t nxk_attention_workspace(const int32_t * h_doc_len, int n_docs, int) {
-    return attn::n_items(h_doc_len, n_docs) * sizeof(attn::Item);
+size_t nxk_attention_workspace(const int32_t * h_doc_len, int n_docs, int half) {
+    const size_t items = attn::n_items(h_doc_len, n_docs, attn::QT3) * sizeof(attn::Item);
+    return (items + 255) / 256 * 256 + attn::scratch_plan(h_doc_len, n_docs, half).bytes;
 }
 
 int nxk_attention(const float * q, const float * k, const float * v, int T, int H, int G, int D, int half,
@@ -289,18 +467,28 @@ int nxk_attention(const float * q, const float * k, const float * v, int T, int 
     if (rep != 1 && rep != 2 && rep != 4) return NXK_EINVAL;     // 64 * rep threads per block
     if (T == 0 || n_docs == 0) return NXK_OK;
     std::vector<attn::Item> items;
-    attn::plan(h_doc_start, h_doc_len, n_docs, half, items);
-    const size_t bytes = items.size() * sizeof(attn::Item);
-    if (!workspace || workspace_bytes < bytes) return NXK_EINVAL;
+    attn::plan(h_doc_start, h_doc_len, n_docs, half, attn::QT3, items);
+    const attn::Scratch sp = attn::scratch_plan(h_doc_len, n_docs, half);
+    const size_t item_bytes = (items.size() * sizeof(attn::Item) + 255) / 256 * 256;
+    if (!workspace || workspace_bytes < item_bytes + sp.bytes) return NXK_EINVAL;
     cudaStream_t s = (cudaStream_t) stream;
     // from pageable memory: staged by CUDA before the call returns, so `items` may go
-    if (cudaMemcpyAsync(workspace, items.data(), bytes, cudaMemcpyHostToDevice, s) != cudaSuccess) return NXK_ELAUNCH;
-    const dim3 grid((unsigned) items.size(), (unsigned) G);
+    if (cudaMemcpyAsync(workspace, items.data(), items.size() * sizeof(attn::Item), cudaMemcpyHostToDevice, s) !=
+        cudaSuccess) {
+        return NXK_ELAUNCH;
+    }
     const attn::Item * it = (const attn::Item *) workspace;
+    float * scratch = (float *) ((char *) workspace + item_bytes);
+    const long long n_units = (long long) items.size() * G;
+    if (n_units > INT32_MAX) return NXK_EINVAL;
+    const unsigned grid = (unsigned) std::min<long long>(n_units, sp.slots);
     switch (rep) {
-        case 1: attn::attn_kernel<1><<<grid, attn::QT * 2, 0, s>>>(q, k, v, out, it, scale, doc_start, doc_len, T, H, half); break;
-        case 2: attn::attn_kernel<2><<<grid, attn::QT * 4, 0, s>>>(q, k, v, out, it, scale, doc_start, doc_len, T, H, half); break;
-        default: attn::attn_kernel<4><<<grid, attn::QT * 8, 0, s>>>(q, k, v, out, it, scale, doc_start, doc_len, T, H, half); break;
+        case 1: attn::attn_scored_kernel<1><<<grid, attn::QT3 * 1, 0, s>>>(q, k, v, out, it, (int) n_units, G, scale,
+                    doc_start, doc_len, T, H, half, scratch, sp.slot_keys); break;
+        case 2: attn::attn_scored_kernel<2><<<grid, attn::QT3 * 2, 0, s>>>(q, k, v, out, it, (int) n_units, G, scale,
+                    doc_start, doc_len, T, H, half, scratch, sp.slot_keys); break;
+        default: attn::attn_scored_kernel<4><<<grid, attn::QT3 * 4, 0, s>>>(q, k, v, out, it, (int) n_units, G, scale,
+                    doc_start, doc_len, T, H, half, scratch, sp.slot_keys); break;
     }
     return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
 }
