@@ -287,45 +287,53 @@ attn_scored_kernel(const float * __restrict__ q, const float * __restrict__ k, c
         const float * kg = k + (size_t) g * T * D;
         const float * vg = v + (size_t) g * T * D;
 
-        // ---- pass 1: every score once (stored), and their maximum
+        // ---- pass 1: every score once (stored), and their maximum.  Lanes l and l+4 of
+        // the 8-lane accumulator run as one packed pair (f32x2 FMA, each component an
+        // IEEE fused multiply-add); key rows sit in shared memory interleaved to match.
         float m = -INFINITY;
         {
-            float qr[D];
+            float2 q2[8][4];            // q2[r][i] = (q[8r+i], q[8r+4+i])
             const float * qp = q + (size_t) (valid ? t : it.q0) * H * D + (size_t) h * D;
 #pragma unroll
-            for (int d4 = 0; d4 < D / 4; ++d4) {
-                const float4 x = *(const float4 *) (qp + 4 * d4);
-                qr[4 * d4] = x.x; qr[4 * d4 + 1] = x.y; qr[4 * d4 + 2] = x.z; qr[4 * d4 + 3] = x.w;
+            for (int r8 = 0; r8 < 8; ++r8) {
+                const float4 x0 = *(const float4 *) (qp + 8 * r8), x1 = *(const float4 *) (qp + 8 * r8 + 4);
+                q2[r8][0] = make_float2(x0.x, x1.x); q2[r8][1] = make_float2(x0.y, x1.y);
+                q2[r8][2] = make_float2(x0.z, x1.z); q2[r8][3] = make_float2(x0.w, x1.w);
             }
             for (int kt = it.k0; kt < it.k1; kt += KT) {
                 const int nk = min(KT, it.k1 - kt);
-                for (int i = threadIdx.x; i < KT * D / 4; i += NT) {
-                    const int j = i / (D / 4), d4 = i % (D / 4);
-                    ((float4 *) Ks[j])[d4] = j < nk ? ((const float4 *) (kg + (size_t) (kt + j) * D))[d4]
-                                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int i = threadIdx.x; i < KT * D / 8; i += NT) {
+                    const int j = i / (D / 8), r8 = i % (D / 8);
+                    float4 k0 = make_float4(0.f, 0.f, 0.f, 0.f), k1 = k0;
+                    if (j < nk) {
+                        k0 = ((const float4 *) (kg + (size_t) (kt + j) * D))[2 * r8];
+                        k1 = ((const float4 *) (kg + (size_t) (kt + j) * D))[2 * r8 + 1];
+                    }
+                    ((float4 *) Ks[j])[2 * r8] = make_float4(k0.x, k1.x, k0.y, k1.y);
+                    ((float4 *) Ks[j])[2 * r8 + 1] = make_float4(k0.z, k1.z, k0.w, k1.w);
                 }
                 __syncthreads();
                 for (int j = 0; j < nk; ++j) {
-                    float a[8];
+                    float2 a[4];                // a[i] = (lane i, lane i+4)
 #pragma unroll
                     for (int r8 = 0; r8 < 8; ++r8) {
-                        const float4 k0 = ((const float4 *) Ks[j])[2 * r8];
-                        const float4 k1 = ((const float4 *) Ks[j])[2 * r8 + 1];
-                        const float kk[8] = { k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w };
+                        const float4 p0 = ((const float4 *) Ks[j])[2 * r8];
+                        const float4 p1 = ((const float4 *) Ks[j])[2 * r8 + 1];
+                        const float2 kk[4] = { make_float2(p0.x, p0.y), make_float2(p0.z, p0.w),
+                                               make_float2(p1.x, p1.y), make_float2(p1.z, p1.w) };
 #pragma unroll
-                        for (int l = 0; l < 8; ++l) {
-                            a[l] = r8 == 0 ? __fmul_rn(qr[l], kk[l]) : __fmaf_rn(qr[8 * r8 + l], kk[l], a[l]);
-                        }
+                        for (int i = 0; i < 4; ++i) a[i] = r8 == 0 ? __fmul2_rn(q2[0][i], kk[i]) : __ffma2_rn(q2[r8][i], kk[i], a[i]);
                     }
                     const int kj = kt + j;
                     float s;
                     if (kj < full_end) {
-                        const float tt = __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3])),
-                                                   __fadd_rn(__fadd_rn(a[4], a[5]), __fadd_rn(a[6], a[7])));
-                        s = __fmul_rn(tt, sc);
+                        // ((a0+a1)+(a2+a3)) + ((a4+a5)+(a6+a7)), both halves at once
+                        const float2 h = __fadd2_rn(__fadd2_rn(a[0], a[1]), __fadd2_rn(a[2], a[3]));
+                        s = __fmul_rn(__fadd_rn(h.x, h.y), sc);
                     } else {
-                        const float tt = __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[4]), __fadd_rn(a[2], a[6])),
-                                                   __fadd_rn(__fadd_rn(a[1], a[5]), __fadd_rn(a[3], a[7])));
+                        // hsum256: ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7))
+                        const float tt = __fadd_rn(__fadd_rn(__fadd_rn(a[0].x, a[0].y), __fadd_rn(a[2].x, a[2].y)),
+                                                   __fadd_rn(__fadd_rn(a[1].x, a[1].y), __fadd_rn(a[3].x, a[3].y)));
                         s = __fmul_rn(sc, tt);
                     }
                     if (kj >= lo && kj < hi) {
@@ -352,10 +360,10 @@ attn_scored_kernel(const float * __restrict__ q, const float * __restrict__ k, c
         }
         const float inv = __fdiv_rn(1.0f, sum);
 
-        // ---- pass 3: o[d] = fma(e_j * inv, v_j[d], o[d]) over the keys in order
-        float o[D];
+        // ---- pass 3: o[d] = fma(e_j * inv, v_j[d], o[d]) over the keys in order (dims in packed pairs)
+        float2 o[D / 2];
 #pragma unroll
-        for (int d = 0; d < D; ++d) o[d] = 0.0f;
+        for (int d = 0; d < D / 2; ++d) o[d] = make_float2(0.0f, 0.0f);
         for (int kt = it.k0; kt < it.k1; kt += KT) {
             const int nk = min(KT, it.k1 - kt);
             for (int i = threadIdx.x; i < KT * D / 4; i += NT) {
@@ -369,13 +377,12 @@ attn_scored_kernel(const float * __restrict__ q, const float * __restrict__ k, c
                 if (kj >= lo && kj < hi) {
                     const float x = __fsub_rn(sc_base[(size_t) (kj - it.k0) * NT + threadIdx.x], m);
                     const float c = __fmul_rn(kj < full_end ? exp8(x) : exp_tail(x), inv);
+                    const float2 c2 = make_float2(c, c);
 #pragma unroll
                     for (int d4 = 0; d4 < D / 4; ++d4) {
                         const float4 vv = ((const float4 *) Vs[j])[d4];
-                        o[4 * d4]     = __fmaf_rn(c, vv.x, o[4 * d4]);
-                        o[4 * d4 + 1] = __fmaf_rn(c, vv.y, o[4 * d4 + 1]);
-                        o[4 * d4 + 2] = __fmaf_rn(c, vv.z, o[4 * d4 + 2]);
-                        o[4 * d4 + 3] = __fmaf_rn(c, vv.w, o[4 * d4 + 3]);
+                        o[2 * d4]     = __ffma2_rn(c2, make_float2(vv.x, vv.y), o[2 * d4]);
+                        o[2 * d4 + 1] = __ffma2_rn(c2, make_float2(vv.z, vv.w), o[2 * d4 + 1]);
                     }
                 }
             }
@@ -385,7 +392,7 @@ attn_scored_kernel(const float * __restrict__ q, const float * __restrict__ k, c
             float4 * op = (float4 *) (out + (size_t) t * H * D + (size_t) h * D);
 #pragma unroll
             for (int d4 = 0; d4 < D / 4; ++d4) {
-                op[d4] = make_float4(o[4 * d4], o[4 * d4 + 1], o[4 * d4 + 2], o[4 * d4 + 3]);
+                op[d4] = make_float4(o[2 * d4].x, o[2 * d4].y, o[2 * d4 + 1].x, o[2 * d4 + 1].y);
             }
         }
     }

@@ -43,8 +43,12 @@ constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BKB, B_BYTES = BN * BKB, STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 32 * (2 + EPI_WARPS);
-constexpr int TMEM_COLS = 2 * BN;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /* alignment */ + 256 /* barriers */;
+constexpr int ACC = 4;                              // TMEM accumulators (one per 256-input block in flight)
+constexpr int TMEM_COLS = ACC * BN;                 // all 512 columns
+constexpr int MAX_BLK = 12;                         // K <= 3072
+constexpr int SW_BYTES = EPI_WARPS * MAX_BLK * 64 * 4;   // each epilogue warp's 64 columns of weight scales
+constexpr int OUT_BYTES = EPI_WARPS * 32 * 64 * 4;       // each epilogue warp's 32 x 64 output slice (2 swizzled boxes)
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + SW_BYTES + 1024 /* alignment */ + 256 /* barriers */;
 constexpr uint32_t IDESC = idesc_i8(BM, BN);
 
 enum : int { ERR_PRODUCER = 0x101, ERR_MMA = 0x102, ERR_EPILOGUE = 0x103 };
@@ -55,17 +59,21 @@ struct Args {
     const float * res;
     float * out;
     int T, N, K, n_blk, n_chunks, tiles_n, n_tiles;
+    int accumulate;          // 1: out += result (the residual is `out` itself), by TMA reduce-add
 };
 
 __global__ void __launch_bounds__(THREADS, 1)
-gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, const Args a) {
+gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+           const __grid_constant__ CUtensorMap tm_out, const Args a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
     uint8_t * sA = smem;
     uint8_t * sB = smem + STAGES * A_BYTES;
-    uint64_t * bars = (uint64_t *) (sB + STAGES * B_BYTES);
-    uint64_t * full = bars, * empty = bars + STAGES, * accf = bars + 2 * STAGES, * acce = bars + 2 * STAGES + 2;
-    uint32_t * tmem_slot = (uint32_t *) (bars + 2 * STAGES + 4);
+    float * so = (float *) (sB + STAGES * B_BYTES);                   // [EPI_WARPS][2][32 rows][32 floats], 1024-aligned
+    float * sw_s = (float *) ((uint8_t *) so + OUT_BYTES);            // [EPI_WARPS][MAX_BLK][64]
+    uint64_t * bars = (uint64_t *) ((uint8_t *) sw_s + SW_BYTES);
+    uint64_t * full = bars, * empty = bars + STAGES, * accf = bars + 2 * STAGES, * acce = bars + 2 * STAGES + ACC;
+    uint32_t * tmem_slot = (uint32_t *) (bars + 2 * STAGES + 2 * ACC);
     volatile int * abort_flag = (volatile int *) (tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -74,7 +82,7 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
             mbar_init(smem_u32(&full[s]), 1);
             mbar_init(smem_u32(&empty[s]), 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < ACC; ++b) {
             mbar_init(smem_u32(&accf[b]), 1);
             mbar_init(smem_u32(&acce[b]), EPI_WARPS);
         }
@@ -82,6 +90,7 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
         fence_barrier_init();
         tma_prefetch_desc(&tm_a);
         tma_prefetch_desc(&tm_b);
+        tma_prefetch_desc(&tm_out);
     }
     if (warp == 1) {
         tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
@@ -124,7 +133,7 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
                 for (int b = 0; ok && b < a.n_blk; ++b, ++kb) {
-                    const uint32_t acc = kb & 1, use = kb >> 1;
+                    const uint32_t acc = kb % ACC, use = kb / ACC;
                     if (use > 0 && !mbar_wait(smem_u32(&acce[acc]), (use - 1) & 1)) { ok = false; break; }
                     if (*abort_flag) { ok = false; break; }
                     tc_fence_after();
@@ -151,23 +160,31 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
                 atomicExch(&g_error, ERR_MMA);
             }
             // the last MMAs complete before TMEM is released
-            if (kb > 0) mbar_wait(smem_u32(&accf[(kb - 1) & 1]), ((kb - 1) >> 1) & 1);
+            if (kb > 0) mbar_wait(smem_u32(&accf[(kb - 1) % ACC]), ((kb - 1) / ACC) & 1);
         }
     } else {
         // ------------------------------------------------------------ epilogue
         const int quad = warp & 3, halfc = (warp - 2) >> 2;
         const int row = 32 * quad + lane;
+        // this warp's private copy of its 64 columns' weight scales: only __syncwarp
+        // orders it, so no cross-warp barrier (which could not time out) is needed
+        float * sws = sw_s + (warp - 2) * MAX_BLK * 64;
         uint32_t kb = 0;
         bool ok = true;
         for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
             const int m0 = (tile / a.tiles_n) * BM, n0 = (tile % a.tiles_n) * BN;
             const int t = m0 + row;
             const int nc = n0 + 64 * halfc;
-            float f[64];
+            __syncwarp();
+            if (nc < a.N) {
+                for (int i = lane; i < a.n_blk * 64; i += 32) sws[i] = a.sw[(size_t) (i >> 6) * a.N + nc + (i & 63)];
+            }
+            __syncwarp();
+            float2 f[32];
 #pragma unroll
-            for (int c = 0; c < 64; ++c) f[c] = 0.0f;
+            for (int c = 0; c < 32; ++c) f[c] = make_float2(0.0f, 0.0f);
             for (int b = 0; b < a.n_blk; ++b, ++kb) {
-                const uint32_t acc = kb & 1, use = kb >> 1;
+                const uint32_t acc = kb % ACC, use = kb / ACC;
                 const bool got = mbar_wait(smem_u32(&accf[acc]), use & 1) && !*abort_flag;
                 if (!__all_sync(0xffffffffu, got)) { ok = false; break; }   // warp-uniform
                 tc_fence_after();
@@ -181,32 +198,63 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
                 if (lane == 0) mbar_arrive(smem_u32(&acce[acc]));
                 if (nc >= a.N) continue;                                   // columns past N (N % 64 == 0)
                 const float sxb = t < a.T ? a.sx[(size_t) t * a.n_blk + b] : 0.0f;
-                const float * swp = a.sw + (size_t) b * a.N + nc;
+                const float2 sx2 = make_float2(sxb, sxb);
+                const float2 nmagic = make_float2(-12582912.0f, -12582912.0f);   // x - m == x + (-m) exactly
+                const float4 * swp = (const float4 *) (sws + b * 64);
+                // f = fma(float(S) * sx, sw, f) per column, two columns per packed instruction;
+                // float(S) exact via the 1.5 * 2^23 bias (|S| <= 2^22)
 #pragma unroll
-                for (int c = 0; c < 32; ++c) {
-                    f[c] = __fmaf_rn(__fmul_rn(i2f_exact((int32_t) r0[c]), sxb), __ldg(swp + c), f[c]);
+                for (int c4 = 0; c4 < 8; ++c4) {
+                    const float4 w = swp[c4];
+                    const float2 s0 = __fadd2_rn(make_float2(__int_as_float((int) r0[4 * c4] + 0x4B400000),
+                                                             __int_as_float((int) r0[4 * c4 + 1] + 0x4B400000)), nmagic);
+                    const float2 s1 = __fadd2_rn(make_float2(__int_as_float((int) r0[4 * c4 + 2] + 0x4B400000),
+                                                             __int_as_float((int) r0[4 * c4 + 3] + 0x4B400000)), nmagic);
+                    f[2 * c4]     = __ffma2_rn(__fmul2_rn(s0, sx2), make_float2(w.x, w.y), f[2 * c4]);
+                    f[2 * c4 + 1] = __ffma2_rn(__fmul2_rn(s1, sx2), make_float2(w.z, w.w), f[2 * c4 + 1]);
                 }
 #pragma unroll
-                for (int c = 0; c < 32; ++c) {
-                    f[32 + c] = __fmaf_rn(__fmul_rn(i2f_exact((int32_t) r1[c]), sxb), __ldg(swp + 32 + c), f[32 + c]);
+                for (int c4 = 0; c4 < 8; ++c4) {
+                    const float4 w = swp[8 + c4];
+                    const float2 s0 = __fadd2_rn(make_float2(__int_as_float((int) r1[4 * c4] + 0x4B400000),
+                                                             __int_as_float((int) r1[4 * c4 + 1] + 0x4B400000)), nmagic);
+                    const float2 s1 = __fadd2_rn(make_float2(__int_as_float((int) r1[4 * c4 + 2] + 0x4B400000),
+                                                             __int_as_float((int) r1[4 * c4 + 3] + 0x4B400000)), nmagic);
+                    f[16 + 2 * c4]     = __ffma2_rn(__fmul2_rn(s0, sx2), make_float2(w.x, w.y), f[16 + 2 * c4]);
+                    f[16 + 2 * c4 + 1] = __ffma2_rn(__fmul2_rn(s1, sx2), make_float2(w.z, w.w), f[16 + 2 * c4 + 1]);
                 }
             }
             if (!ok) break;
-            if (t < a.T && nc < a.N) {
-                float * o = a.out + (size_t) t * a.N + nc;
-                const float * rr = a.res ? a.res + (size_t) t * a.N + nc : nullptr;
+            if (nc < a.N) {
+                // this warp's 32 x 64 slice -> shared memory (two 32 x 32 boxes in the 128-byte
+                // swizzle: 16-byte chunk c of row r at chunk c ^ (r % 8)) -> one TMA store or
+                // reduce-add per box; rows past T are clipped by the tensor map
+                float * sbox = so + (warp - 2) * 2048;
+                if (lane == 0) bulk_wait_read();               // the previous tile's boxes have been read
+                __syncwarp();
 #pragma unroll
-                for (int c = 0; c < 64; c += 4) {
-                    float4 v = make_float4(f[c], f[c + 1], f[c + 2], f[c + 3]);
-                    if (rr) {
-                        const float4 r4 = *(const float4 *) (rr + c);
-                        v.x = __fadd_rn(r4.x, v.x); v.y = __fadd_rn(r4.y, v.y);
-                        v.z = __fadd_rn(r4.z, v.z); v.w = __fadd_rn(r4.w, v.w);
+                for (int hb = 0; hb < 2; ++hb) {
+                    float * rowp = sbox + hb * 1024 + lane * 32;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const float2 lo = f[16 * hb + 2 * c], hi = f[16 * hb + 2 * c + 1];
+                        *(float4 *) (rowp + 4 * (c ^ (lane & 7))) = make_float4(lo.x, lo.y, hi.x, hi.y);
                     }
-                    *(float4 *) (o + c) = v;
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    const int y = m0 + 32 * quad;
+#pragma unroll
+                    for (int hb = 0; hb < 2; ++hb) {
+                        if (a.accumulate) tma_reduce_add_2d(&tm_out, nc + 32 * hb, y, smem_u32(sbox + hb * 1024));
+                        else              tma_store_2d(&tm_out, nc + 32 * hb, y, smem_u32(sbox + hb * 1024));
+                    }
+                    bulk_commit();
                 }
             }
         }
+        if (lane == 0) bulk_wait_all();
         if (!ok) {
             *abort_flag = 1;
             atomicExch(&g_error, ERR_EPILOGUE);
@@ -255,6 +303,19 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
+// rows x N fp32, boxes of 32 rows x 32 floats (128 bytes) in the 128-byte swizzle
+bool make_out_map(CUtensorMap * m, const void * base, uint64_t rows, uint64_t N) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = { (cuuint64_t) N, (cuuint64_t) rows };
+    cuuint64_t strides[1] = { (cuuint64_t) N * 4 };
+    cuuint32_t box[2] = { 32, 32 };
+    cuuint32_t estr[2] = { 1, 1 };
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // rows x K bytes, K-contiguous, boxes of 128 rows x 128 bytes in the 128-byte swizzle
 bool make_map(CUtensorMap * m, const void * base, uint64_t rows, uint64_t K) {
     auto fn = encode_fn();
@@ -288,24 +349,35 @@ int nxk_linear_i8(const int8_t * xq, const float * sx, int T, const int8_t * w8,
     // TMA: K-byte row pitch a multiple of 16, 16-byte aligned bases; each epilogue
     // warp owns 64 output columns, so N must be a multiple of 64
     if (T < 0 || K <= 0 || N <= 0 || (K & 31) || (N & 63) || !xq || !w8 || !sx || !sw || !out) return NXK_EINVAL;
+    if ((K + I8_BLOCK - 1) / I8_BLOCK > MAX_BLK) return NXK_EINVAL;
     if (((uintptr_t) xq & 15) || ((uintptr_t) w8 & 15) || ((uintptr_t) out & 15)) return NXK_EINVAL;
     if (res && ((uintptr_t) res & 15)) return NXK_EINVAL;
     if (T == 0) return NXK_OK;
-    CUtensorMap ma, mb;
-    if (!make_map(&ma, xq, (uint64_t) T, (uint64_t) K) || !make_map(&mb, w8, (uint64_t) N, (uint64_t) K)) return NXK_ELAUNCH;
+    CUtensorMap ma, mb, mo;
+    if (!make_map(&ma, xq, (uint64_t) T, (uint64_t) K) || !make_map(&mb, w8, (uint64_t) N, (uint64_t) K) ||
+        !make_out_map(&mo, out, (uint64_t) T, (uint64_t) N)) {
+        return NXK_ELAUNCH;
+    }
+    // a residual other than `out` itself is copied into `out` first: the kernel accumulates in place
+    if (res && res != out &&
+        cudaMemcpyAsync(out, res, sizeof(float) * (size_t) T * N, cudaMemcpyDeviceToDevice, (cudaStream_t) stream) !=
+            cudaSuccess) {
+        return NXK_ELAUNCH;
+    }
     static std::once_flag attr_once;
     std::call_once(attr_once, []() {
         cudaFuncSetAttribute(gemm_i8_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     });
     Args a;
     a.sx = sx; a.sw = sw; a.res = res; a.out = out;
+    a.accumulate = res ? 1 : 0;
     a.T = T; a.N = N; a.K = K;
     a.n_blk = (K + I8_BLOCK - 1) / I8_BLOCK;
     a.n_chunks = (K + BKB - 1) / BKB;
     a.tiles_n = (N + BN - 1) / BN;
     a.n_tiles = ((T + BM - 1) / BM) * a.tiles_n;
     const int grid = min(a.n_tiles, sm_count());
-    gemm_i8_tc<<<grid, THREADS, SMEM_BYTES, (cudaStream_t) stream>>>(ma, mb, a);
+    gemm_i8_tc<<<grid, THREADS, SMEM_BYTES, (cudaStream_t) stream>>>(ma, mb, mo, a);
     return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
 }
 

@@ -840,8 +840,7 @@ int run_encoder(nextera_context & c, const Batch & b, float rope0_base, const in
         fw.linear(pre + "c_gate.weight", Q1, Q1s, T, nullptr, gl);
         fw.mark(PROF_ROWS);
         fw.rows(nxk_gate(gl, z, T, C, nullptr, Q1, Q1s, s), "gate");
-        fw.linear(pre + "c_proj.weight", Q1, Q1s, T, X, X2);
-        std::swap(X, X2);
+        fw.linear(pre + "c_proj.weight", Q1, Q1s, T, X, X);       // x += c_proj(...), in place
     };
 
     for (int l = 0; l < n_layer && fw.ok; ++l) {
@@ -866,8 +865,7 @@ int run_encoder(nextera_context & c, const Batch & b, float rope0_base, const in
             fw.mark(PROF_ROWS);
             fw.rows(nxk_lily_state(Fa, Fb, Fc, k2->taps.as<float>(), k2->k, L.row_doc, L.start, L.len, T, C, nullptr,
                                    Q1, Q1s, s), "lily_state");
-            fw.linear(pre + "c_proj.weight", Q1, Q1s, T, X, X2);
-            std::swap(X, X2);
+            fw.linear(pre + "c_proj.weight", Q1, Q1s, T, X, X);      // x += c_proj(...), in place
         } else if (mt == MIX_SWA || mt == MIX_ATTN) {
             const bool swa = mt == MIX_SWA;
             const int half = swa ? std::max(1, hp.swa_window / 2) : -1;
@@ -905,8 +903,7 @@ int run_encoder(nextera_context & c, const Batch & b, float rope0_base, const in
         fw.linear(blk + "mlp.c_fc.weight", Q2, Q2s, T, nullptr, U);
         fw.mark(PROF_ROWS);
         fw.rows(nxk_relu_sqr(U, T, I, nullptr, Q1, Q1s, s), "relu_sqr");
-        fw.linear(blk + "mlp.c_proj.weight", Q1, Q1s, T, X, X2);
-        std::swap(X, X2);
+        fw.linear(blk + "mlp.c_proj.weight", Q1, Q1s, T, X, X);      // x += c_proj(...), in place
     }
     if (!fw.ok) return 3;
     float * hidden = X;
