@@ -250,8 +250,8 @@ attn_kernel(const float * __restrict__ q, const float * __restrict__ k, const fl
 // memory), computes every score once, and keeps it in a per-CTA scratch slot in
 // global memory (sized for the longest key range of the launch; L2-resident for
 // the band layers).  Pass 2 walks the thread's own scores in groups of 8 for the
-// exp-sum; pass 3 re-derives each weight from the stored score and accumulates
-// the values.  Work units (tile, KV head) are spread over a persistent grid,
+// exp-sum and leaves each exp in place of its score; pass 3 scales them by
+// 1/sum and accumulates the values.  Work units (tile, KV head) are spread over a persistent grid,
 // longest first.
 // ---------------------------------------------------------------------------
 constexpr int QT3 = 64;            // queries per work unit
@@ -266,6 +266,7 @@ attn_scored_kernel(const float * __restrict__ q, const float * __restrict__ k, c
     constexpr int NT = QT3 * REP;
     __shared__ __align__(16) float Ks[KT][D];
     __shared__ __align__(16) float Vs[KT][D];
+    __shared__ float Cw[KT][NT];                                        // the tile's softmax weights
     float * sc_base = scratch + (size_t) blockIdx.x * slot_keys * NT;   // [key - k0][thread]
 
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
@@ -313,6 +314,7 @@ attn_scored_kernel(const float * __restrict__ q, const float * __restrict__ k, c
                     ((float4 *) Ks[j])[2 * r8 + 1] = make_float4(k0.z, k1.z, k0.w, k1.w);
                 }
                 __syncthreads();
+#pragma unroll 2
                 for (int j = 0; j < nk; ++j) {
                     float2 a[4];                // a[i] = (lane i, lane i+4)
 #pragma unroll
@@ -345,18 +347,40 @@ attn_scored_kernel(const float * __restrict__ q, const float * __restrict__ k, c
             }
         }
 
-        // ---- pass 2: exp256 over whole groups of 8, summed per lane in key order; then the tail
+        // ---- pass 2: e = exp256(s - m) over whole groups of 8, summed per lane in key order,
+        // then the tail with the C library's exp; every e overwrites its score for pass 3
         float sum;
         {
             float vs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            const float * sp = sc_base + (size_t) (lo - it.k0) * NT + threadIdx.x;
-            for (int j = 0; j < (n & ~7); j += 8) {
+            float * sp = sc_base + (size_t) (lo - it.k0) * NT + threadIdx.x;
+            const int nf = n & ~7;
+            int j = 0;
+            for (; j + 16 <= nf; j += 16) {                 // two groups per trip: 16 loads in flight
+                float x[16];
 #pragma unroll
-                for (int l = 0; l < 8; ++l) vs[l] = __fadd_rn(vs[l], exp8(__fsub_rn(sp[(size_t) (j + l) * NT], m)));
+                for (int l = 0; l < 16; ++l) x[l] = sp[(size_t) (j + l) * NT];
+#pragma unroll
+                for (int l = 0; l < 16; ++l) {
+                    const float e = exp8(__fsub_rn(x[l], m));
+                    vs[l & 7] = __fadd_rn(vs[l & 7], e);
+                    sp[(size_t) (j + l) * NT] = e;
+                }
+            }
+            for (; j < nf; j += 8) {
+#pragma unroll
+                for (int l = 0; l < 8; ++l) {
+                    const float e = exp8(__fsub_rn(sp[(size_t) (j + l) * NT], m));
+                    vs[l] = __fadd_rn(vs[l], e);
+                    sp[(size_t) (j + l) * NT] = e;
+                }
             }
             sum = __fadd_rn(__fadd_rn(__fadd_rn(vs[0], vs[4]), __fadd_rn(vs[2], vs[6])),
                             __fadd_rn(__fadd_rn(vs[1], vs[5]), __fadd_rn(vs[3], vs[7])));
-            for (int j = n & ~7; j < n; ++j) sum = __fadd_rn(sum, exp_tail(__fsub_rn(sp[(size_t) j * NT], m)));
+            for (j = nf; j < n; ++j) {
+                const float e = exp_tail(__fsub_rn(sp[(size_t) j * NT], m));
+                sum = __fadd_rn(sum, e);
+                sp[(size_t) j * NT] = e;
+            }
         }
         const float inv = __fdiv_rn(1.0f, sum);
 
@@ -372,11 +396,19 @@ attn_scored_kernel(const float * __restrict__ q, const float * __restrict__ k, c
                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
             }
             __syncthreads();
+            // this thread's weights for the tile's keys -> Cw (0 outside its range), then the values
+#pragma unroll 8
+            for (int j = 0; j < KT; ++j) {
+                const int kj = kt + j;
+                float c = 0.0f;
+                if (j < nk && kj >= lo && kj < hi) c = __fmul_rn(sc_base[(size_t) (kj - it.k0) * NT + threadIdx.x], inv);
+                Cw[j][threadIdx.x] = c;
+            }
+            __syncthreads();
             for (int j = 0; j < nk; ++j) {
                 const int kj = kt + j;
                 if (kj >= lo && kj < hi) {
-                    const float x = __fsub_rn(sc_base[(size_t) (kj - it.k0) * NT + threadIdx.x], m);
-                    const float c = __fmul_rn(kj < full_end ? exp8(x) : exp_tail(x), inv);
+                    const float c = Cw[j][threadIdx.x];
                     const float2 c2 = make_float2(c, c);
 #pragma unroll
                     for (int d4 = 0; d4 < D / 4; ++d4) {
@@ -488,7 +520,17 @@ int nxk_attention(const float * q, const float * k, const float * v, int T, int 
     float * scratch = (float *) ((char *) workspace + item_bytes);
     const long long n_units = (long long) items.size() * G;
     if (n_units > INT32_MAX) return NXK_EINVAL;
-    const unsigned grid = (unsigned) std::min<long long>(n_units, sp.slots);
+    // persistent grid: no more CTAs than can be resident at once (each owns a scratch slot)
+    int dev = 0, sms = 148, per_sm = 1;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    switch (rep) {
+        case 1: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn::attn_scored_kernel<1>, attn::QT3, 0); break;
+        case 2: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn::attn_scored_kernel<2>, attn::QT3 * 2, 0); break;
+        default: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn::attn_scored_kernel<4>, attn::QT3 * 4, 0); break;
+    }
+    const long long resident = (long long) std::max(per_sm, 1) * std::max(sms, 1);
+    const unsigned grid = (unsigned) std::min<long long>(std::min<long long>(n_units, sp.slots), resident);
     switch (rep) {
         case 1: attn::attn_scored_kernel<1><<<grid, attn::QT3 * 1, 0, s>>>(q, k, v, out, it, (int) n_units, G, scale,
                     doc_start, doc_len, T, H, half, scratch, sp.slot_keys); break;
