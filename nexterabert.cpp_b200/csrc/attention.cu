@@ -244,187 +244,333 @@ attn_kernel(const float * __restrict__ q, const float * __restrict__ k, const fl
 }
 
 // ---------------------------------------------------------------------------
-// Stored-score kernel (used by nxk_attention).  Same arithmetic as attn_kernel;
-// the difference is where the scores live.  One thread owns one (query, head) and
-// all 64 lanes of its dot products (q in registers, keys broadcast from shared
-// memory), computes every score once, and keeps it in a per-CTA scratch slot in
-// global memory (sized for the longest key range of the launch; L2-resident for
-// the band layers).  Pass 2 walks the thread's own scores in groups of 8 for the
-// exp-sum and leaves each exp in place of its score; pass 3 scales them by
-// 1/sum and accumulates the values.  Work units (tile, KV head) are spread over a persistent grid,
-// longest first.
+// Tiled kernel (used by nxk_attention).  Same arithmetic and order as
+// attn_kernel; what changes is which thread does which operation.  A work unit
+// is (64-query tile, KV head g) with the H/G query heads that share g; its
+// scores live in a per-CTA scratch slot in global memory, [key - k0][query,
+// head], L2-resident for the band layers.
+//   pass 1  every score once, in register tiles: a thread owns 4 queries x 4
+//           keys and runs the 8 lane chains of NEXTERA_DOT64 one lane after
+//           the other (dims l, 8 + l, ..., 56 + l), folding each finished lane
+//           into the full-group tree ((a0+a1)+(a2+a3)) + ((a4+a5)+(a6+a7)) as
+//           it completes.  Queries and keys sit transposed in shared memory
+//           ([dim][query], [dim][key]), so one float4 of each feeds 16 FMAs.
+//           Partial maxima over the keys in whole groups go to shared memory.
+//   pass 2  two threads per (query, head): the tail keys (the n % 8 after the
+//           last whole group) are recomputed with the hsum256 tree, then the
+//           exp-sum runs with lanes 0-3 of every group on one thread and lanes
+//           4-7 on the other, each exp written over its score; 1 / sum.
+//   pass 3  register tiles of 4 queries x 8 dims: o = fma(e * inv, v, o) over
+//           the keys in order; the tile's weights are staged in shared memory,
+//           zero outside a query's range (fma(0, v, o) leaves o unchanged).
 // ---------------------------------------------------------------------------
 constexpr int QT3 = 64;            // queries per work unit
 
 template <int REP>
-__global__ void __launch_bounds__(QT3 * REP)
-attn_scored_kernel(const float * __restrict__ q, const float * __restrict__ k, const float * __restrict__ v,
-                   float * __restrict__ out, const Item * __restrict__ items, int n_units, int G,
-                   const float * __restrict__ scale, const int32_t * __restrict__ doc_start,
-                   const int32_t * __restrict__ doc_len, int T, int H, int half, float * __restrict__ scratch,
-                   int slot_keys) {
-    constexpr int NT = QT3 * REP;
-    __shared__ __align__(16) float Ks[KT][D];
-    __shared__ __align__(16) float Vs[KT][D];
-    __shared__ float Cw[KT][NT];                                        // the tile's softmax weights
-    float * sc_base = scratch + (size_t) blockIdx.x * slot_keys * NT;   // [key - k0][thread]
+constexpr int tiled_smem_floats() {
+    return REP * D * QT3 + D * KT + KT * D + KT * QT3 * REP + QT3 * REP;
+}
+
+template <int REP>
+__global__ void __launch_bounds__(128 * REP, 4 / REP)
+attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, const float * __restrict__ v,
+                  float * __restrict__ out, const Item * __restrict__ items, int n_units, int G,
+                  const float * __restrict__ scale, const int32_t * __restrict__ doc_start,
+                  const int32_t * __restrict__ doc_len, int T, int H, int half, float * __restrict__ scratch,
+                  int slot_keys) {
+    constexpr int NT = 128 * REP;
+    constexpr int NQH = QT3 * REP;                                  // (query, head) pairs of a unit
+    extern __shared__ __align__(16) float smem[];
+    float (*Qs)[QT3] = reinterpret_cast<float (*)[QT3]>(smem);                       // [REP * D][QT3]
+    float (*Ks)[KT] = reinterpret_cast<float (*)[KT]>(smem + REP * D * QT3);         // [D][KT]
+    float (*Vs)[D] = reinterpret_cast<float (*)[D]>(smem + REP * D * QT3 + D * KT);  // [KT][D]
+    float (*Cw)[NQH] = reinterpret_cast<float (*)[NQH]>(smem + REP * D * QT3 + 2 * D * KT);   // [KT][NQH]
+    float * mx = &Cw[0][0];                                        // [8][NQH], passes 1-2 only
+    float * invs = smem + REP * D * QT3 + 2 * D * KT + KT * NQH;    // [NQH]
+    float * sc_base = scratch + (size_t) blockIdx.x * slot_keys * NQH;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int hq = warp >> 2, w4 = warp & 3;                       // 4 warps per query head
+    const int qa = 32 * (w4 & 1) + 4 * (lane & 7);                 // the thread's 4 queries
+    const int kb = 16 * (w4 >> 1) + 4 * (lane >> 3);               // pass 1: its 4 keys of a tile
+    const int kgrp = kb >> 2;                                      // 0..7
+    const int db = 32 * (w4 >> 1) + 8 * (lane >> 3);               // pass 3: its 8 dims
+    const int p_qh = tid >> 1, p_sub = tid & 1;                    // pass 2: the pair
+    const int p_h = p_qh / QT3, p_qi = p_qh % QT3;
+    const int c_qh = tid % NQH;                                    // pass 3: weight column it fills
 
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
         const Item it = items[u / G];
         const int g = u % G;
-        const int hq = threadIdx.x / QT3, qi = threadIdx.x % QT3;
-        const int h = g * REP + hq;
-        const int t = it.q0 + qi;
-        const bool valid = t < it.q1;
-        int lo = doc_start[it.doc], hi = lo + doc_len[it.doc];
-        if (half >= 0) {
-            lo = max(lo, t - half);
-            hi = min(hi, t + half + 1);
-        }
-        if (!valid) { lo = it.k0; hi = it.k0; }
-        const int n = hi - lo;
-        const int full_end = lo + (n & ~7);
         const float sc = scale[it.doc];
+        const int dlo = doc_start[it.doc], dhi = dlo + doc_len[it.doc];
         const float * kg = k + (size_t) g * T * D;
         const float * vg = v + (size_t) g * T * D;
+        // the key range [lo, hi) of query row q0 + qi (empty past q1)
+        auto range = [&](int qi, int & lo, int & hi) {
+            const int t = it.q0 + qi;
+            lo = dlo;
+            hi = dhi;
+            if (half >= 0) {
+                lo = max(lo, t - half);
+                hi = min(hi, t + half + 1);
+            }
+            if (t >= it.q1) { lo = it.k0; hi = it.k0; }
+        };
 
-        // ---- pass 1: every score once (stored), and their maximum.  Lanes l and l+4 of
-        // the 8-lane accumulator run as one packed pair (f32x2 FMA, each component an
-        // IEEE fused multiply-add); key rows sit in shared memory interleaved to match.
-        float m = -INFINITY;
-        {
-            float2 q2[8][4];            // q2[r][i] = (q[8r+i], q[8r+4+i])
-            const float * qp = q + (size_t) (valid ? t : it.q0) * H * D + (size_t) h * D;
-#pragma unroll
-            for (int r8 = 0; r8 < 8; ++r8) {
-                const float4 x0 = *(const float4 *) (qp + 8 * r8), x1 = *(const float4 *) (qp + 8 * r8 + 4);
-                q2[r8][0] = make_float2(x0.x, x1.x); q2[r8][1] = make_float2(x0.y, x1.y);
-                q2[r8][2] = make_float2(x0.z, x1.z); q2[r8][3] = make_float2(x0.w, x1.w);
-            }
-            for (int kt = it.k0; kt < it.k1; kt += KT) {
-                const int nk = min(KT, it.k1 - kt);
-                for (int i = threadIdx.x; i < KT * D / 8; i += NT) {
-                    const int j = i / (D / 8), r8 = i % (D / 8);
-                    float4 k0 = make_float4(0.f, 0.f, 0.f, 0.f), k1 = k0;
-                    if (j < nk) {
-                        k0 = ((const float4 *) (kg + (size_t) (kt + j) * D))[2 * r8];
-                        k1 = ((const float4 *) (kg + (size_t) (kt + j) * D))[2 * r8 + 1];
-                    }
-                    ((float4 *) Ks[j])[2 * r8] = make_float4(k0.x, k1.x, k0.y, k1.y);
-                    ((float4 *) Ks[j])[2 * r8 + 1] = make_float4(k0.z, k1.z, k0.w, k1.w);
-                }
-                __syncthreads();
-#pragma unroll 2
-                for (int j = 0; j < nk; ++j) {
-                    float2 a[4];                // a[i] = (lane i, lane i+4)
-#pragma unroll
-                    for (int r8 = 0; r8 < 8; ++r8) {
-                        const float4 p0 = ((const float4 *) Ks[j])[2 * r8];
-                        const float4 p1 = ((const float4 *) Ks[j])[2 * r8 + 1];
-                        const float2 kk[4] = { make_float2(p0.x, p0.y), make_float2(p0.z, p0.w),
-                                               make_float2(p1.x, p1.y), make_float2(p1.z, p1.w) };
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) a[i] = r8 == 0 ? __fmul2_rn(q2[0][i], kk[i]) : __ffma2_rn(q2[r8][i], kk[i], a[i]);
-                    }
-                    const int kj = kt + j;
-                    float s;
-                    if (kj < full_end) {
-                        // ((a0+a1)+(a2+a3)) + ((a4+a5)+(a6+a7)), both halves at once
-                        const float2 h = __fadd2_rn(__fadd2_rn(a[0], a[1]), __fadd2_rn(a[2], a[3]));
-                        s = __fmul_rn(__fadd_rn(h.x, h.y), sc);
-                    } else {
-                        // hsum256: ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7))
-                        const float tt = __fadd_rn(__fadd_rn(__fadd_rn(a[0].x, a[0].y), __fadd_rn(a[2].x, a[2].y)),
-                                                   __fadd_rn(__fadd_rn(a[1].x, a[1].y), __fadd_rn(a[3].x, a[3].y)));
-                        s = __fmul_rn(sc, tt);
-                    }
-                    if (kj >= lo && kj < hi) {
-                        m = (m < s) ? s : m;
-                        sc_base[(size_t) (kj - it.k0) * NT + threadIdx.x] = s;
-                    }
-                }
-                __syncthreads();
-            }
+        // queries, transposed (zeros past q1); the previous unit's last reads of Qs
+        // are in pass 2, which a barrier closes
+        for (int i = tid; i < REP * QT3 * (D / 4); i += NT) {
+            const int qi = i % QT3, r = i / QT3;
+            const int h = r / (D / 4), d4 = r % (D / 4);
+            const int t = it.q0 + qi;
+            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (t < it.q1) x = *(const float4 *) (q + ((size_t) t * H + (size_t) g * REP + h) * D + 4 * d4);
+            Qs[h * D + 4 * d4 + 0][qi] = x.x;
+            Qs[h * D + 4 * d4 + 1][qi] = x.y;
+            Qs[h * D + 4 * d4 + 2][qi] = x.z;
+            Qs[h * D + 4 * d4 + 3][qi] = x.w;
         }
 
-        // ---- pass 2: e = exp256(s - m) over whole groups of 8, summed per lane in key order,
-        // then the tail with the C library's exp; every e overwrites its score for pass 3
-        float sum;
-        {
-            float vs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            float * sp = sc_base + (size_t) (lo - it.k0) * NT + threadIdx.x;
-            const int nf = n & ~7;
-            int j = 0;
-            for (; j + 16 <= nf; j += 16) {                 // two groups per trip: 16 loads in flight
-                float x[16];
+        // ---- pass 1
+        int lo4[4], fe4[4];
+        float ml[4];
 #pragma unroll
-                for (int l = 0; l < 16; ++l) x[l] = sp[(size_t) (j + l) * NT];
-#pragma unroll
-                for (int l = 0; l < 16; ++l) {
-                    const float e = exp8(__fsub_rn(x[l], m));
-                    vs[l & 7] = __fadd_rn(vs[l & 7], e);
-                    sp[(size_t) (j + l) * NT] = e;
-                }
-            }
-            for (; j < nf; j += 8) {
-#pragma unroll
-                for (int l = 0; l < 8; ++l) {
-                    const float e = exp8(__fsub_rn(sp[(size_t) (j + l) * NT], m));
-                    vs[l] = __fadd_rn(vs[l], e);
-                    sp[(size_t) (j + l) * NT] = e;
-                }
-            }
-            sum = __fadd_rn(__fadd_rn(__fadd_rn(vs[0], vs[4]), __fadd_rn(vs[2], vs[6])),
-                            __fadd_rn(__fadd_rn(vs[1], vs[5]), __fadd_rn(vs[3], vs[7])));
-            for (j = nf; j < n; ++j) {
-                const float e = exp_tail(__fsub_rn(sp[(size_t) j * NT], m));
-                sum = __fadd_rn(sum, e);
-                sp[(size_t) j * NT] = e;
-            }
+        for (int a = 0; a < 4; ++a) {
+            int lo, hi;
+            range(qa + a, lo, hi);
+            lo4[a] = lo;
+            fe4[a] = lo + ((hi - lo) & ~7);
+            ml[a] = -INFINITY;
         }
-        const float inv = __fdiv_rn(1.0f, sum);
-
-        // ---- pass 3: o[d] = fma(e_j * inv, v_j[d], o[d]) over the keys in order (dims in packed pairs)
-        float2 o[D / 2];
+        const float (*Qh)[QT3] = Qs + hq * D;
+        // key tiles: the next tile's rows are loaded into registers while this one is used
+        constexpr int KPT = KT * D / 4 / NT;
+        float4 kp[KPT];
+        auto kload = [&](int kt) {
 #pragma unroll
-        for (int d = 0; d < D / 2; ++d) o[d] = make_float2(0.0f, 0.0f);
+            for (int z = 0; z < KPT; ++z) {
+                const int i = tid + z * NT, j = i % KT, d4 = i / KT;
+                kp[z] = kt + j < it.k1 ? *(const float4 *) (kg + (size_t) (kt + j) * D + 4 * d4)
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        };
+        kload(it.k0);
         for (int kt = it.k0; kt < it.k1; kt += KT) {
             const int nk = min(KT, it.k1 - kt);
-            for (int i = threadIdx.x; i < KT * D / 4; i += NT) {
-                const int j = i / (D / 4), d4 = i % (D / 4);
-                ((float4 *) Vs[j])[d4] = j < nk ? ((const float4 *) (vg + (size_t) (kt + j) * D))[d4]
-                                                : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-            __syncthreads();
-            // this thread's weights for the tile's keys -> Cw (0 outside its range), then the values
-#pragma unroll 8
-            for (int j = 0; j < KT; ++j) {
-                const int kj = kt + j;
-                float c = 0.0f;
-                if (j < nk && kj >= lo && kj < hi) c = __fmul_rn(sc_base[(size_t) (kj - it.k0) * NT + threadIdx.x], inv);
-                Cw[j][threadIdx.x] = c;
-            }
-            __syncthreads();
-            for (int j = 0; j < nk; ++j) {
-                const int kj = kt + j;
-                if (kj >= lo && kj < hi) {
-                    const float c = Cw[j][threadIdx.x];
-                    const float2 c2 = make_float2(c, c);
+            __syncthreads();                                       // Ks free; Qs written
 #pragma unroll
-                    for (int d4 = 0; d4 < D / 4; ++d4) {
-                        const float4 vv = ((const float4 *) Vs[j])[d4];
-                        o[2 * d4]     = __ffma2_rn(c2, make_float2(vv.x, vv.y), o[2 * d4]);
-                        o[2 * d4 + 1] = __ffma2_rn(c2, make_float2(vv.z, vv.w), o[2 * d4 + 1]);
+            for (int z = 0; z < KPT; ++z) {
+                const int i = tid + z * NT, j = i % KT, d4 = i / KT;
+                Ks[4 * d4 + 0][j] = kp[z].x;
+                Ks[4 * d4 + 1][j] = kp[z].y;
+                Ks[4 * d4 + 2][j] = kp[z].z;
+                Ks[4 * d4 + 3][j] = kp[z].w;
+            }
+            __syncthreads();
+            if (kt + KT < it.k1) kload(kt + KT);
+            float y0123[4][4], x45[4][4], x6[4][4], x01[4][4], x2[4][4], x0[4][4], x4[4][4];
+#pragma unroll
+            for (int l = 0; l < 8; ++l) {
+                float acc[4][4];
+#pragma unroll
+                for (int r = 0; r < 8; ++r) {
+                    const int d = 8 * r + l;
+                    const float4 qv = *(const float4 *) &Qh[d][qa];
+                    const float4 kv = *(const float4 *) &Ks[d][kb];
+                    const float qq[4] = {qv.x, qv.y, qv.z, qv.w};
+                    const float kk[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+                    for (int a = 0; a < 4; ++a)
+#pragma unroll
+                        for (int b2 = 0; b2 < 4; ++b2)
+                            acc[a][b2] = r == 0 ? __fmul_rn(qq[a], kk[b2]) : __fmaf_rn(qq[a], kk[b2], acc[a][b2]);
+                }
+#pragma unroll
+                for (int a = 0; a < 4; ++a)
+#pragma unroll
+                    for (int b2 = 0; b2 < 4; ++b2) {
+                        const float c = acc[a][b2];
+                        switch (l) {
+                            case 0: x0[a][b2] = c; break;
+                            case 1: x01[a][b2] = __fadd_rn(x0[a][b2], c); break;
+                            case 2: x2[a][b2] = c; break;
+                            case 3: y0123[a][b2] = __fadd_rn(x01[a][b2], __fadd_rn(x2[a][b2], c)); break;
+                            case 4: x4[a][b2] = c; break;
+                            case 5: x45[a][b2] = __fadd_rn(x4[a][b2], c); break;
+                            case 6: x6[a][b2] = c; break;
+                            default: {
+                                const float s = __fmul_rn(__fadd_rn(y0123[a][b2],
+                                                                    __fadd_rn(x45[a][b2], __fadd_rn(x6[a][b2], c))), sc);
+                                x0[a][b2] = s;                     // the finished score
+                            }
+                        }
                     }
+            }
+#pragma unroll
+            for (int b2 = 0; b2 < 4; ++b2) {
+                const int kj = kt + kb + b2;
+                if (kb + b2 < nk) {
+                    *(float4 *) (sc_base + (size_t) (kj - it.k0) * NQH + hq * QT3 + qa) =
+                        make_float4(x0[0][b2], x0[1][b2], x0[2][b2], x0[3][b2]);
+#pragma unroll
+                    for (int a = 0; a < 4; ++a) {
+                        if (kj >= lo4[a] && kj < fe4[a]) ml[a] = (ml[a] < x0[a][b2]) ? x0[a][b2] : ml[a];
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int a = 0; a < 4; ++a) mx[kgrp * NQH + hq * QT3 + qa + a] = ml[a];
+        __syncthreads();
+
+        // ---- pass 2
+        {
+            int lo, hi;
+            range(p_qi, lo, hi);
+            const int n = hi - lo, fe = lo + (n & ~7);
+            float m = -INFINITY;
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+                const float x = mx[r * NQH + p_qh];
+                m = (m < x) ? x : m;
+            }
+            float * sp = sc_base + p_qh;
+            if (p_sub == 0) {
+                // tail keys: hsum256 ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7)), then * scale
+                for (int kj = fe; kj < hi; ++kj) {
+                    const float4 * kr = (const float4 *) (kg + (size_t) kj * D);
+                    float a8[8];
+#pragma unroll
+                    for (int r = 0; r < 8; ++r) {
+                        const float4 k0 = kr[2 * r], k1 = kr[2 * r + 1];
+                        const float kk[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+#pragma unroll
+                        for (int l = 0; l < 8; ++l) {
+                            const float qv = Qs[p_h * D + 8 * r + l][p_qi];
+                            a8[l] = r == 0 ? __fmul_rn(qv, kk[l]) : __fmaf_rn(qv, kk[l], a8[l]);
+                        }
+                    }
+                    const float tt = __fadd_rn(__fadd_rn(__fadd_rn(a8[0], a8[4]), __fadd_rn(a8[2], a8[6])),
+                                               __fadd_rn(__fadd_rn(a8[1], a8[5]), __fadd_rn(a8[3], a8[7])));
+                    const float s = __fmul_rn(sc, tt);
+                    sp[(size_t) (kj - it.k0) * NQH] = s;
+                    m = (m < s) ? s : m;
+                }
+            }
+            {
+                const float o = __shfl_xor_sync(0xffffffffu, m, 1);
+                m = (m < o) ? o : m;
+            }
+            // whole groups: this thread's lanes 4 * sub .. 4 * sub + 3, summed per lane in key order
+            float vs[4] = {0.f, 0.f, 0.f, 0.f};
+            const int ng = n >> 3;
+            float * gp = sp + (size_t) (lo - it.k0 + 4 * p_sub) * NQH;
+            int gi = 0;
+            for (; gi + 4 <= ng; gi += 4) {                        // 16 loads in flight
+                float x[16];
+#pragma unroll
+                for (int z = 0; z < 16; ++z) x[z] = gp[(size_t) (8 * (gi + (z >> 2)) + (z & 3)) * NQH];
+#pragma unroll
+                for (int z = 0; z < 16; ++z) {
+                    const float e = exp8(__fsub_rn(x[z], m));
+                    vs[z & 3] = __fadd_rn(vs[z & 3], e);
+                    gp[(size_t) (8 * (gi + (z >> 2)) + (z & 3)) * NQH] = e;
+                }
+            }
+            for (; gi < ng; ++gi) {
+#pragma unroll
+                for (int z = 0; z < 4; ++z) {
+                    float * p = gp + (size_t) (8 * gi + z) * NQH;
+                    const float e = exp8(__fsub_rn(*p, m));
+                    vs[z] = __fadd_rn(vs[z], e);
+                    *p = e;
+                }
+            }
+            // sum = ((v0+v4)+(v2+v6)) + ((v1+v5)+(v3+v7)); lanes 4-7 are the partner's 0-3
+            float w[4];
+#pragma unroll
+            for (int z = 0; z < 4; ++z) w[z] = __shfl_xor_sync(0xffffffffu, vs[z], 1);
+            if (p_sub == 0) {
+                float sum = __fadd_rn(__fadd_rn(__fadd_rn(vs[0], w[0]), __fadd_rn(vs[2], w[2])),
+                                      __fadd_rn(__fadd_rn(vs[1], w[1]), __fadd_rn(vs[3], w[3])));
+                for (int kj = fe; kj < hi; ++kj) {
+                    float * p = sp + (size_t) (kj - it.k0) * NQH;
+                    const float e = exp_tail(__fsub_rn(*p, m));
+                    sum = __fadd_rn(sum, e);
+                    *p = e;
+                }
+                invs[p_qh] = __fdiv_rn(1.0f, sum);
+            }
+        }
+        __syncthreads();
+
+        // ---- pass 3
+        int c_lo, c_hi;
+        range(c_qh % QT3, c_lo, c_hi);
+        const float c_inv = invs[c_qh];
+        float2 o[4][4];                                            // [query][dim pair]
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int z = 0; z < 4; ++z) o[a][z] = make_float2(0.0f, 0.0f);
+        // value rows and exps of the next tile are loaded into registers while this one is used
+        constexpr int VPT = KT * D / 4 / NT, EPT = KT * NQH / NT;
+        float4 vp[VPT];
+        float ep[EPT];
+        auto vload = [&](int kt) {
+#pragma unroll
+            for (int z = 0; z < VPT; ++z) {
+                const int i = tid + z * NT, j = i / (D / 4), d4 = i % (D / 4);
+                vp[z] = kt + j < it.k1 ? ((const float4 *) (vg + (size_t) (kt + j) * D))[d4]
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int z = 0; z < EPT; ++z) {
+                const int kj = kt + tid / NQH + z * (NT / NQH);
+                ep[z] = (kj < it.k1 && kj >= c_lo && kj < c_hi) ? sc_base[(size_t) (kj - it.k0) * NQH + c_qh] : 0.0f;
+            }
+        };
+        vload(it.k0);
+        for (int kt = it.k0; kt < it.k1; kt += KT) {
+            const int nk = min(KT, it.k1 - kt);
+#pragma unroll
+            for (int z = 0; z < VPT; ++z) {
+                const int i = tid + z * NT, j = i / (D / 4), d4 = i % (D / 4);
+                ((float4 *) Vs[j])[d4] = vp[z];
+            }
+            // weight = e * inv inside the query's range, 0 outside
+#pragma unroll
+            for (int z = 0; z < EPT; ++z) {
+                const int j = tid / NQH + z * (NT / NQH), kj = kt + j;
+                Cw[j][c_qh] = (kj < it.k1 && kj >= c_lo && kj < c_hi) ? __fmul_rn(ep[z], c_inv) : 0.0f;
+            }
+            __syncthreads();
+            if (kt + KT < it.k1) vload(kt + KT);
+#pragma unroll 2
+            for (int j = 0; j < nk; ++j) {
+                const float4 cv = *(const float4 *) &Cw[j][hq * QT3 + qa];
+                const float4 v0 = *(const float4 *) &Vs[j][db];
+                const float4 v1 = *(const float4 *) &Vs[j][db + 4];
+                const float cc[4] = {cv.x, cv.y, cv.z, cv.w};
+                const float2 vv[4] = {make_float2(v0.x, v0.y), make_float2(v0.z, v0.w),
+                                      make_float2(v1.x, v1.y), make_float2(v1.z, v1.w)};
+#pragma unroll
+                for (int a = 0; a < 4; ++a) {
+                    const float2 c2 = make_float2(cc[a], cc[a]);
+#pragma unroll
+                    for (int z = 0; z < 4; ++z) o[a][z] = __ffma2_rn(c2, vv[z], o[a][z]);
                 }
             }
             __syncthreads();
         }
-        if (valid) {
-            float4 * op = (float4 *) (out + (size_t) t * H * D + (size_t) h * D);
 #pragma unroll
-            for (int d4 = 0; d4 < D / 4; ++d4) {
-                op[d4] = make_float4(o[2 * d4].x, o[2 * d4].y, o[2 * d4 + 1].x, o[2 * d4 + 1].y);
+        for (int a = 0; a < 4; ++a) {
+            const int t = it.q0 + qa + a;
+            if (t < it.q1) {
+                float4 * op = (float4 *) (out + ((size_t) t * H + (size_t) g * REP + hq) * D + db);
+                op[0] = make_float4(o[a][0].x, o[a][0].y, o[a][1].x, o[a][1].y);
+                op[1] = make_float4(o[a][2].x, o[a][2].y, o[a][3].x, o[a][3].y);
             }
         }
     }
@@ -456,9 +602,9 @@ size_t n_items(const int32_t * len, int n_docs, int qt) {
     return n;
 }
 
-// Score scratch of the stored-score kernel: one slot per resident CTA, each
-// holding (longest key range) x (threads) floats; threads sized for 4 heads per
-// KV head (the most this build runs).  Slots: 4 per SM, at least one per SM,
+// Score scratch of the tiled kernel: one slot per resident CTA, each holding
+// (longest key range) x (query, head) floats, sized for 4 query heads per KV
+// head (the most this build runs).  Slots: 4 per SM, at least one per SM,
 // and no more than fit in 8 GiB.
 constexpr int SLOTS_PER_SM = 4;
 constexpr size_t SCRATCH_BUDGET = (size_t) 8 << 30;
@@ -524,20 +670,22 @@ int nxk_attention(const float * q, const float * k, const float * v, int T, int 
     int dev = 0, sms = 148, per_sm = 1;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    auto launch = [&](auto kernel, int rep_) {
+        const int threads = 128 * rep_;
+        const size_t smem_bytes = sizeof(float) * (size_t) (rep_ == 1 ? attn::tiled_smem_floats<1>()
+                                                            : rep_ == 2 ? attn::tiled_smem_floats<2>()
+                                                                        : attn::tiled_smem_floats<4>());
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem_bytes);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem_bytes);
+        const long long resident = (long long) std::max(per_sm, 1) * std::max(sms, 1);
+        const unsigned grid = (unsigned) std::min<long long>(std::min<long long>(n_units, sp.slots), resident);
+        kernel<<<grid, threads, smem_bytes, s>>>(q, k, v, out, it, (int) n_units, G, scale, doc_start, doc_len, T, H,
+                                                 half, scratch, sp.slot_keys);
+    };
     switch (rep) {
-        case 1: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn::attn_scored_kernel<1>, attn::QT3, 0); break;
-        case 2: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn::attn_scored_kernel<2>, attn::QT3 * 2, 0); break;
-        default: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn::attn_scored_kernel<4>, attn::QT3 * 4, 0); break;
-    }
-    const long long resident = (long long) std::max(per_sm, 1) * std::max(sms, 1);
-    const unsigned grid = (unsigned) std::min<long long>(std::min<long long>(n_units, sp.slots), resident);
-    switch (rep) {
-        case 1: attn::attn_scored_kernel<1><<<grid, attn::QT3 * 1, 0, s>>>(q, k, v, out, it, (int) n_units, G, scale,
-                    doc_start, doc_len, T, H, half, scratch, sp.slot_keys); break;
-        case 2: attn::attn_scored_kernel<2><<<grid, attn::QT3 * 2, 0, s>>>(q, k, v, out, it, (int) n_units, G, scale,
-                    doc_start, doc_len, T, H, half, scratch, sp.slot_keys); break;
-        default: attn::attn_scored_kernel<4><<<grid, attn::QT3 * 4, 0, s>>>(q, k, v, out, it, (int) n_units, G, scale,
-                    doc_start, doc_len, T, H, half, scratch, sp.slot_keys); break;
+        case 1: launch(attn::attn_tiled_kernel<1>, 1); break;
+        case 2: launch(attn::attn_tiled_kernel<2>, 2); break;
+        default: launch(attn::attn_tiled_kernel<4>, 4); break;
     }
     return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
 }
