@@ -83,6 +83,13 @@ NEXTERA_API int nxk_qk_prep(const float * x, const float * alpha, const float * 
                             const int32_t * doc_start, int T, int H, int D, int head_major, float * out,
                             void * stream);
 NEXTERA_API int nxk_head_major(const float * x, int T, int H, int D, float * out, void * stream);
+/* q, k and v of one mixer from its fused projection x [T][ldx] (columns: H q heads, G k heads,
+ * G v heads): qk_prep on q (token-major [T][H][D]) and on k (head-major [G][T][D]), v copied
+ * head-major; D must be 64.  Same values as nxk_qk_prep / nxk_head_major on the split columns. */
+NEXTERA_API int nxk_qkv_prep(const float * x, int ldx, const float * q_alpha, const float * q_beta,
+                             const float * k_alpha, const float * k_beta, const float * cos_t,
+                             const float * sin_t, const int32_t * row_doc, const int32_t * doc_start,
+                             int T, int H, int G, int D, float * q, float * k, float * v, void * stream);
 NEXTERA_API int nxk_block_mean(const float * h, const float * g, int C, int block,
                                const int32_t * doc_start, const int32_t * doc_len,
                                const int32_t * bdoc_start, const int32_t * brow_doc, int n_brows,

@@ -39,6 +39,8 @@ enum cls_task { CLS_NONE, CLS_SEQUENCE, CLS_CHOICE, CLS_TOKEN, CLS_QA };
 const char * const CLS_NAMES[] = { "", "sequence-classification", "multiple-choice", "token-classification",
                                    "question-answering" };
 constexpr int I8_BLOCK = 256;
+// the load-time concatenation of an attention mixer's c_q, c_k and c_v (no such tensor in a file)
+const char * const QKV_NAME = "c_qkv.weight#fused";
 
 struct hparams {
     int32_t n_vocab = 0, n_embd = 0, n_layer = 0, n_inter = 0, n_head = 0, n_kv_head = 0, head_dim = 0;
@@ -213,7 +215,35 @@ bool check(int rc, const char * what) {
     return true;
 }
 
-size_t align_up(size_t n, size_t a) { return (n + a - 1) / a * a; }
+
+// Concatenates expanded int8 weights with the same input width along their output rows into
+// one weight `name` (scales [block][row] likewise); the parts are released.
+bool fuse_rows(nextera_context & c, const std::vector<std::string> & parts, const std::string & name) {
+    int n_in = -1, n_out = 0;
+    for (const std::string & p : parts) {
+        auto it = c.i8.find(p);
+        if (it == c.i8.end() || (n_in >= 0 && it->second.n_in != n_in)) return false;
+        n_in = it->second.n_in;
+        n_out += it->second.n_out;
+    }
+    I8Weight & f = c.i8[name];
+    f.n_in = n_in;
+    f.n_out = n_out;
+    const int n_blk = (n_in + I8_BLOCK - 1) / I8_BLOCK;
+    if (!f.w.alloc((size_t) n_in * n_out) || !f.scale.alloc(sizeof(float) * (size_t) n_blk * n_out)) return false;
+    size_t row = 0;
+    for (const std::string & p : parts) {
+        const I8Weight & w = c.i8.at(p);
+        cudaMemcpyAsync(f.w.as<int8_t>() + row * n_in, w.w.p, (size_t) w.n_in * w.n_out, cudaMemcpyDeviceToDevice,
+                        c.stream);
+        cudaMemcpy2DAsync(f.scale.as<float>() + row, sizeof(float) * n_out, w.scale.p, sizeof(float) * w.n_out,
+                          sizeof(float) * w.n_out, n_blk, cudaMemcpyDeviceToDevice, c.stream);
+        row += w.n_out;
+    }
+    if (cudaStreamSynchronize(c.stream) != cudaSuccess) return false;
+    for (const std::string & p : parts) c.i8.erase(p);
+    return true;
+}
 
 } // namespace
 
@@ -452,13 +482,25 @@ struct nextera_context * nextera_load(const char * path, struct nextera_params p
         }
     }
 
+    // attention mixers: c_q, c_k and c_v become one weight, rows in that order, so one GEMM
+    // computes all three projections
+    const size_t n_file_linears = c->i8.size();
+    for (int l = 0; l < hp.n_layer; ++l) {
+        if (hp.block_types[l] == MIX_LILY) continue;
+        const std::string pre = "blocks." + std::to_string(l) + ".attn.";
+        if (!fuse_rows(*c, {pre + "c_q.weight", pre + "c_k.weight", pre + "c_v.weight"}, pre + QKV_NAME)) {
+            fprintf(stderr, "nexterabert: cannot build the fused q/k/v weight of layer %d\n", l);
+            return nullptr;
+        }
+    }
+
     cudaDeviceProp prop;
     cudaGetDeviceProperties(&prop, c->device);
     char info[512];
     snprintf(info, sizeof(info),
              "CUDA = 1 | device = %s (sm_%d%d, %d SMs) | linear layers: %d int8 (tcgen05 kind::i8), 0 ggml repack | "
              "custom ops: CUDA sm_100a",
-             prop.name, prop.major, prop.minor, prop.multiProcessorCount, (int) c->i8.size());
+             prop.name, prop.major, prop.minor, prop.multiProcessorCount, (int) n_file_linears);
     c->sysinfo = info;
     if (params.verbosity > 0) {
         const double ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t_start).count();
@@ -703,7 +745,7 @@ bool ensure_arena(nextera_context & c, const Batch & b) {
     const hparams & hp = c.hp;
     const int64_t T = std::max<int64_t>(b.T, 1), C = hp.n_embd, I = hp.n_inter;
     const int64_t HD = (int64_t) hp.n_head * hp.head_dim, GD = (int64_t) hp.n_kv_head * hp.head_dim;
-    const int64_t wide = std::max<int64_t>(I, HD + 2 * GD);
+    const int64_t wide = std::max<int64_t>(I, 2 * (HD + 2 * GD));     // q, k, v and their fused projection
     const int64_t nb_C = (C + I8_BLOCK - 1) / I8_BLOCK, nb_W = (std::max(I, C) + I8_BLOCK - 1) / I8_BLOCK;
     bool ok = c.X.reserve(sizeof(float) * T * C) && c.X2.reserve(sizeof(float) * T * C) &&
               c.U.reserve(sizeof(float) * T * wide) && c.Fa.reserve(sizeof(float) * T * C) &&
@@ -817,17 +859,15 @@ int run_encoder(nextera_context & c, const Batch & b, float rope0_base, const in
         float * q = U;
         float * k = U + (size_t) rows * H * D;
         float * v = k + (size_t) rows * G * D;
-        fw.linear(pre + "c_q.weight", hq, hsx, rows, nullptr, Fc);
+        // c_q, c_k, c_v as one GEMM over their concatenated rows (each output column is the
+        // same dot product as in the separate layers), then DyT + RoPE and the layouts in one pass
+        const int ld = (H + 2 * G) * D;
+        float * qkv = v + (size_t) rows * G * D;
+        fw.linear(pre + QKV_NAME, hq, hsx, rows, nullptr, qkv);
         fw.mark(PROF_ROWS);
-        fw.rows(nxk_qk_prep(Fc, fw.p(pre + "q_norm.alpha"), fw.p(pre + "q_norm.beta"), c.rope_cos[rope].as<float>(),
-                            c.rope_sin[rope].as<float>(), row_doc, start, rows, H, D, 0, q, s), "qk_prep(q)");
-        fw.linear(pre + "c_k.weight", hq, hsx, rows, nullptr, Fc);
-        fw.mark(PROF_ROWS);
-        fw.rows(nxk_qk_prep(Fc, fw.p(pre + "k_norm.alpha"), fw.p(pre + "k_norm.beta"), c.rope_cos[rope].as<float>(),
-                            c.rope_sin[rope].as<float>(), row_doc, start, rows, G, D, 1, k, s), "qk_prep(k)");
-        fw.linear(pre + "c_v.weight", hq, hsx, rows, nullptr, Fc);
-        fw.mark(PROF_ROWS);
-        fw.rows(nxk_head_major(Fc, rows, G, D, v, s), "head_major");
+        fw.rows(nxk_qkv_prep(qkv, ld, fw.p(pre + "q_norm.alpha"), fw.p(pre + "q_norm.beta"), fw.p(pre + "k_norm.alpha"),
+                             fw.p(pre + "k_norm.beta"), c.rope_cos[rope].as<float>(), c.rope_sin[rope].as<float>(),
+                             row_doc, start, rows, H, G, D, q, k, v, s), "qkv_prep");
         fw.mark(PROF_ATTN);
         fw.rows(nxk_attention(q, k, v, rows, H, G, D, half, scale, row_doc, start, len, b.n_docs, h_start.data(),
                               h_len.data(), c.attn_ws.p, c.attn_ws.bytes, y, s), "attention");

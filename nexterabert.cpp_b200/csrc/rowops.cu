@@ -1,14 +1,17 @@
 // Row ops, activation quantization, embedding gather, weight expansion,
 // LayerNorm and pooling for sm_100a.
 //
-// All of these are HBM-bound.  The layout is one warp per row: lane L owns the
-// elements 32*i + L, so every load and store of a warp is one contiguous
-// 128-byte segment, and the lane's fma chain over those elements is exactly
-// one lane of the reference's 32-lane dot_f32 accumulator (src/nexterabert.cpp
-// :133-151).  Rows are produced element by element in the reference's
-// operation order and, when the consumer is an int8 linear, quantized per
-// (row, 256-column block) in the same pass (quantize_row, :378-403): the fp32
-// row never touches memory.
+// All of these are HBM-bound.  Elementwise row ops run one warp per row with
+// lane L owning the 8 consecutive columns 256*B + 8*L .. +7 of each 256-column
+// block B (16-byte loads, one 8-byte store of int8 codes); the one reduction
+// along a row that must follow the reference's order, op_rms_norm's dot
+// product, reads the row the other way round first: lane L chains the
+// elements 32*i + L, exactly one lane of the 32-lane dot_f32 accumulator
+// (src/nexterabert.cpp:133-151).  The token convolutions stage their rows and
+// halo in shared memory.  Every value is produced in the reference's operation
+// order and, when the consumer is an int8 linear, quantized per (row,
+// 256-column block) in the same pass (quantize_row, :378-403): the fp32 row
+// never touches memory.
 #include "common.cuh"
 #include "dequant.cuh"
 #include "nextera_kernels.h"
@@ -21,48 +24,17 @@ __device__ int g_error;
 
 constexpr int ROW_THREADS = 256;     // 8 rows per block
 
-// ---------------------------------------------------------------------------
-// generic row emitter: fp32 output, or int8 codes + per-block scales
-// ---------------------------------------------------------------------------
-template <class Op>
-__global__ void __launch_bounds__(ROW_THREADS) row_kernel(Op op, int T, int C, float * __restrict__ out,
-                                                          int8_t * __restrict__ q, float * __restrict__ sx) {
-    const int t = (int) ((blockIdx.x * (size_t) blockDim.x + threadIdx.x) >> 5);
-    const int lane = threadIdx.x & 31;
-    if (t >= T) return;
-    op.prepare(t, lane, C);
-    const int n_i = C >> 5;
-    if (!q) {
-        float * o = out + (size_t) t * C;
-        for (int i = 0; i < n_i; ++i) o[32 * i + lane] = op.value(t, 32 * i + lane, C);
-        return;
-    }
-    const int n_blk = (C + I8_BLOCK - 1) / I8_BLOCK;
-    int8_t * qo = q + (size_t) t * C;
-    for (int B = 0; B < n_blk; ++B) {
-        float v[8];
-        float am = 0.0f;
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int i = 8 * B + u;
-            v[u] = i < n_i ? op.value(t, 32 * i + lane, C) : 0.0f;
-            am = fmaxf(am, fabsf(v[u]));
-        }
-        am = warp_max(am);
-        const float inv = act_inv(am);
-        if (lane == 0) sx[(size_t) t * n_blk + B] = act_scale(am);
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int i = 8 * B + u;
-            if (i < n_i) qo[32 * i + lane] = act_code(v[u], inv);
-        }
-    }
+// eight consecutive floats (16-byte aligned)
+__device__ __forceinline__ void ld8(const float * p, float (&v)[8]) {
+    const float4 a = ((const float4 *) p)[0], b = ((const float4 *) p)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
 struct CopyOp {
     const float * x;
     __device__ void prepare(int, int, int) {}
-    __device__ float value(int t, int c, int C) const { return x[(size_t) t * C + c]; }
+    __device__ void value8(int t, int c0, int C, float (&v)[8]) const { ld8(x + (size_t) t * C + c0, v); }
 };
 
 // op_rms_norm (:464-482): x * (1 / sqrt(dot(x, x) / C + eps)) * g
@@ -81,8 +53,12 @@ struct RmsOp {
         const float dot = warp_dot_tree(acc);
         inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(dot, (float) C), eps)));
     }
-    __device__ float value(int t, int c, int C) const {
-        return __fmul_rn(__fmul_rn(x[(size_t) t * C + c], inv), g[c]);
+    __device__ void value8(int t, int c0, int C, float (&v)[8]) const {
+        float gg[8];
+        ld8(x + (size_t) t * C + c0, v);
+        ld8(g + c0, gg);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], inv), gg[e]);
     }
 };
 
@@ -90,10 +66,13 @@ struct RmsOp {
 struct ReluSqrOp {
     const float * x;
     __device__ void prepare(int, int, int) {}
-    __device__ float value(int t, int c, int C) const {
-        const float v = x[(size_t) t * C + c];
-        const float r = v > 0.0f ? v : 0.0f;
-        return __fmul_rn(r, r);
+    __device__ void value8(int t, int c0, int C, float (&v)[8]) const {
+        ld8(x + (size_t) t * C + c0, v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float r = v[e] > 0.0f ? v[e] : 0.0f;
+            v[e] = __fmul_rn(r, r);
+        }
     }
 };
 
@@ -102,62 +81,12 @@ struct GateOp {
     const float * g;
     const float * y;
     __device__ void prepare(int, int, int) {}
-    __device__ float value(int t, int c, int C) const {
-        const size_t i = (size_t) t * C + c;
-        return __fmul_rn(sigmoid8(g[i]), y[i]);
-    }
-};
-
-// op_dwconv (:528-544): r (or 0) + sum_j w[j][c] * x[t + j - k/2][c] inside the document
-struct DwconvOp {
-    const float * x;
-    const float * r;
-    const float * taps;
-    int k;
-    const int32_t * row_doc;
-    const int32_t * doc_start;
-    const int32_t * doc_len;
-    int lo, hi;
-    __device__ void prepare(int t, int, int) {
-        const int d = row_doc[t];
-        lo = doc_start[d];
-        hi = lo + doc_len[d];
-    }
-    __device__ float value(int t, int c, int C) const {
-        float v = r ? r[(size_t) t * C + c] : 0.0f;
-        for (int j = 0; j < k; ++j) {
-            const int tt = t + j - k / 2;
-            if (tt < lo || tt >= hi) continue;
-            v = __fmaf_rn(taps[(size_t) j * C + c], x[(size_t) tt * C + c], v);
-        }
-        return v;
-    }
-};
-
-// op_lily_state (:548-579): b[t] * sum_j w[j] * (a * x)[t + j - k/2]
-struct LilyOp {
-    const float * a;
-    const float * x;
-    const float * b;
-    const float * taps;
-    int k;
-    const int32_t * row_doc;
-    const int32_t * doc_start;
-    const int32_t * doc_len;
-    int j0, j1;
-    __device__ void prepare(int t, int, int) {
-        const int d = row_doc[t];
-        const int lo = doc_start[d], hi = lo + doc_len[d];
-        j0 = max(0, lo - (t - k / 2));
-        j1 = min(k, hi - (t - k / 2));
-    }
-    __device__ float value(int t, int c, int C) const {
-        float acc = 0.0f;
-        for (int j = j0; j < j1; ++j) {
-            const size_t tt = (size_t) (t + j - k / 2) * C + c;
-            acc = __fmaf_rn(taps[(size_t) j * C + c], __fmul_rn(a[tt], x[tt]), acc);
-        }
-        return __fmul_rn(acc, b[(size_t) t * C + c]);
+    __device__ void value8(int t, int c0, int C, float (&v)[8]) const {
+        float gg[8];
+        ld8(g + (size_t) t * C + c0, gg);
+        ld8(y + (size_t) t * C + c0, v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(sigmoid8(gg[e]), v[e]);
     }
 };
 
@@ -178,13 +107,17 @@ struct BlockMeanOp {
         n = min(block, doc_len[d] - bi * block);
         inv = __fdiv_rn(1.0f, (float) n);
     }
-    __device__ float value(int, int c, int C) const {
-        float acc = 0.0f;
+    __device__ void value8(int, int c0, int C, float (&v)[8]) const {
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         for (int i = 0; i < n; ++i) {
-            const size_t at = (size_t) (ts + i) * C + c;
-            acc = g ? __fmaf_rn(h[at], g[at], acc) : __fmaf_rn(1.0f, h[at], acc);
+            float hh[8], gg[8];
+            ld8(h + (size_t) (ts + i) * C + c0, hh);
+            if (g) ld8(g + (size_t) (ts + i) * C + c0, gg);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] = g ? __fmaf_rn(hh[e], gg[e], acc[e]) : __fmaf_rn(1.0f, hh[e], acc[e]);
         }
-        return __fmul_rn(acc, inv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(acc[e], inv);
     }
 };
 
@@ -201,19 +134,227 @@ struct UpsampleOp {
         const int d = row_doc[t];
         yb = bdoc_start[d] + (t - doc_start[d]) / block;
     }
-    __device__ float value(int t, int c, int C) const {
-        return __fadd_rn(y[(size_t) yb * C + c], r[(size_t) t * C + c]);
+    __device__ void value8(int t, int c0, int C, float (&v)[8]) const {
+        float rr[8];
+        ld8(y + (size_t) yb * C + c0, v);
+        ld8(r + (size_t) t * C + c0, rr);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = __fadd_rn(v[e], rr[e]);
     }
 };
 
+// ---------------------------------------------------------------------------
+// Vectorised row emitter: lane L of the row's warp owns the 8 consecutive
+// columns 256 * B + 8 * L .. + 7 of each 256-column block B, so every input is
+// read with two 16-byte loads and the codes leave as one 8-byte store.  The
+// per-element arithmetic is the scalar emitter's; only the lane that does it
+// changes (the block's amax is a max, independent of order).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t pack4(float a, float b, float c, float d, float inv) {
+    return (uint32_t) (uint8_t) act_code(a, inv) | ((uint32_t) (uint8_t) act_code(b, inv) << 8) |
+           ((uint32_t) (uint8_t) act_code(c, inv) << 16) | ((uint32_t) (uint8_t) act_code(d, inv) << 24);
+}
+
+// one row's 8 values of a 256-column block -> fp32 or codes (+ the block scale from lane 0)
+__device__ __forceinline__ void emit8(const float (&v)[8], bool on, int lane, size_t row_off, int c0, int blk,
+                                      int n_blk, size_t t, float * __restrict__ out, int8_t * __restrict__ q,
+                                      float * __restrict__ sx) {
+    if (!q) {
+        if (on) {
+            float4 * o = (float4 *) (out + row_off + c0);
+            o[0] = make_float4(v[0], v[1], v[2], v[3]);
+            o[1] = make_float4(v[4], v[5], v[6], v[7]);
+        }
+        return;
+    }
+    float am = 0.0f;
+    if (on) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) am = fmaxf(am, fabsf(v[e]));
+    }
+    am = warp_max(am);
+    const float inv = act_inv(am);
+    if (lane == 0) sx[t * n_blk + blk] = act_scale(am);
+    if (on) *(uint2 *) (q + row_off + c0) = make_uint2(pack4(v[0], v[1], v[2], v[3], inv), pack4(v[4], v[5], v[6], v[7], inv));
+}
+
 template <class Op>
-int launch_rows(const Op & op, int T, int C, float * out, int8_t * q, float * sx, cudaStream_t s) {
+__global__ void __launch_bounds__(ROW_THREADS) row8_kernel(Op op, int T, int C, float * __restrict__ out,
+                                                           int8_t * __restrict__ q, float * __restrict__ sx) {
+    const int t = (int) ((blockIdx.x * (size_t) blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
+    if (t >= T) return;
+    op.prepare(t, lane, C);
+    const int n_blk = (C + I8_BLOCK - 1) / I8_BLOCK;
+    for (int B = 0; B < n_blk; ++B) {
+        const int c0 = B * I8_BLOCK + 8 * lane;
+        const bool on = c0 < C;
+        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (on) op.value8(t, c0, C, v);
+        emit8(v, on, lane, (size_t) t * C, c0, B, n_blk, (size_t) t, out, q, sx);
+    }
+}
+
+template <class Op>
+int launch_rows8(const Op & op, int T, int C, float * out, int8_t * q, float * sx, cudaStream_t s) {
     if (T < 0 || C <= 0 || (C & 31) || (!q && !out) || (q && !sx)) return NXK_EINVAL;
     if (T == 0) return NXK_OK;
     const int rows_per_block = ROW_THREADS / 32;
     const unsigned grid = (unsigned) ((T + rows_per_block - 1) / rows_per_block);
-    row_kernel<Op><<<grid, ROW_THREADS, 0, s>>>(op, T, C, out, q, sx);
+    row8_kernel<Op><<<grid, ROW_THREADS, 0, s>>>(op, T, C, out, q, sx);
     return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
+}
+
+// ---------------------------------------------------------------------------
+// Depthwise convolutions along the tokens of a document, tiled: a block owns
+// CONV_ROWS rows x one 256-column block.  The rows it reads (its own plus k-1
+// of halo) are staged in shared memory once, as x (op_dwconv, :528-544) or as
+// the product a * x (op_lily_state, :548-579), with the taps; then each warp
+// runs the tap loop of its rows from shared memory in the reference's order
+// (taps ascending, only those inside the row's document) and emits the row's
+// block as fp32 or codes.
+//   dwconv  v = r (or 0);  v = fma(w[j], x[t + j - k/2], v)
+//   lily    v = 0;         v = fma(w[j], (a * x)[t + j - k/2], v);  v = v * b[t]
+// ---------------------------------------------------------------------------
+constexpr int CONV_ROWS = 32;
+constexpr int CONV_KMAX = 64;
+
+inline size_t conv_smem_bytes(int k) { return sizeof(float) * 256 * (size_t) (CONV_ROWS + 2 * k - 1); }
+
+template <bool LILY>
+__global__ void __launch_bounds__(256) conv_kernel(const float * __restrict__ x, const float * __restrict__ a,
+                                                   const float * __restrict__ r, const float * __restrict__ b,
+                                                   const float * __restrict__ taps, int k,
+                                                   const int32_t * __restrict__ row_doc,
+                                                   const int32_t * __restrict__ doc_start,
+                                                   const int32_t * __restrict__ doc_len, int T, int C,
+                                                   float * __restrict__ out, int8_t * __restrict__ q,
+                                                   float * __restrict__ sx) {
+    extern __shared__ float4 conv_sm[];
+    float * P = (float *) conv_sm;                              // [CONV_ROWS + k - 1][256]
+    const int n_rows = CONV_ROWS + k - 1;
+    float * W = P + (size_t) n_rows * 256;                      // [k][256]
+    const int t0 = blockIdx.x * CONV_ROWS, cb = blockIdx.y * 256;
+    const int ncol = min(256, C - cb);
+    const int hk = k / 2;
+    for (int i = threadIdx.x; i < n_rows * 64; i += blockDim.x) {
+        const int rr = i >> 6, c4 = i & 63;
+        const int tr = t0 - hk + rr;
+        if (tr < 0 || tr >= T || 4 * c4 >= ncol) continue;
+        const size_t off = (size_t) tr * C + cb + 4 * c4;
+        float4 xv = *(const float4 *) (x + off);
+        if (LILY) {
+            const float4 av = *(const float4 *) (a + off);
+            xv = make_float4(__fmul_rn(av.x, xv.x), __fmul_rn(av.y, xv.y), __fmul_rn(av.z, xv.z), __fmul_rn(av.w, xv.w));
+        }
+        ((float4 *) P)[i] = xv;
+    }
+    for (int i = threadIdx.x; i < k * 64; i += blockDim.x) {
+        const int j = i >> 6, c4 = i & 63;
+        if (4 * c4 < ncol) ((float4 *) W)[i] = *(const float4 *) (taps + (size_t) j * C + cb + 4 * c4);
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c0 = 8 * lane;
+    const bool on = c0 < ncol;
+    const int n_blk = (C + I8_BLOCK - 1) / I8_BLOCK;
+    for (int rr = warp; rr < CONV_ROWS; rr += (int) (blockDim.x >> 5)) {
+        const int t = t0 + rr;
+        if (t >= T) break;
+        const int d = row_doc[t];
+        const int lo = doc_start[d], hi = lo + doc_len[d];
+        const int j0 = max(0, lo - (t - hk)), j1 = min(k, hi - (t - hk));
+        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (on) {
+            if (!LILY && r) ld8(r + (size_t) t * C + cb + c0, v);
+            for (int j = j0; j < j1; ++j) {
+                float pv[8], wv[8];
+                ld8(P + (size_t) (rr + j) * 256 + c0, pv);
+                ld8(W + (size_t) j * 256 + c0, wv);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = __fmaf_rn(wv[e], pv[e], v[e]);
+            }
+            if (LILY) {
+                float bv[8];
+                ld8(b + (size_t) t * C + cb + c0, bv);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(v[e], bv[e]);
+            }
+        }
+        emit8(v, on, lane, (size_t) t * C + cb, c0, blockIdx.y, n_blk, (size_t) t, out, q, sx);
+    }
+}
+
+int launch_conv(bool lily, const float * x, const float * a, const float * r, const float * b, const float * taps,
+                int k, const int32_t * row_doc, const int32_t * doc_start, const int32_t * doc_len, int T, int C,
+                float * out, int8_t * q, float * sx, cudaStream_t s) {
+    if (T < 0 || C <= 0 || (C & 31) || k <= 0 || k > CONV_KMAX || (!q && !out) || (q && !sx)) return NXK_EINVAL;
+    if (T == 0) return NXK_OK;
+    const dim3 grid((unsigned) ((T + CONV_ROWS - 1) / CONV_ROWS), (unsigned) ((C + 255) / 256));
+    const size_t smem = conv_smem_bytes(k);
+    if (lily) {
+        cudaFuncSetAttribute(conv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+        conv_kernel<true><<<grid, 256, smem, s>>>(x, a, nullptr, b, taps, k, row_doc, doc_start, doc_len, T, C, out,
+                                                 q, sx);
+    } else {
+        cudaFuncSetAttribute(conv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+        conv_kernel<false><<<grid, 256, smem, s>>>(x, nullptr, r, nullptr, taps, k, row_doc, doc_start, doc_len, T, C,
+                                                  out, q, sx);
+    }
+    return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
+}
+
+// ---------------------------------------------------------------------------
+// q / k / v of one attention mixer from the fused projection [T][H*D + 2*G*D]:
+// q and k heads through qk_prep's DyT + RoPE, q token-major [T][H][D], k and v
+// head-major [G][T][D].  One warp per row (the document position and the RoPE
+// row are looked up once for all heads); D = 64, lane i owns the pair (i, i+32).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) qkv_prep_kernel(const float * __restrict__ x, int ldx,
+                                                       const float * __restrict__ q_alpha,
+                                                       const float * __restrict__ q_beta,
+                                                       const float * __restrict__ k_alpha,
+                                                       const float * __restrict__ k_beta,
+                                                       const float * __restrict__ cos_t,
+                                                       const float * __restrict__ sin_t,
+                                                       const int32_t * __restrict__ row_doc,
+                                                       const int32_t * __restrict__ doc_start, int T, int H, int G,
+                                                       float * __restrict__ q, float * __restrict__ k,
+                                                       float * __restrict__ v) {
+    const int t = (int) ((blockIdx.x * (size_t) blockDim.x + threadIdx.x) >> 5);
+    const int i = threadIdx.x & 31;
+    if (t >= T) return;
+    const int pos = t - doc_start[row_doc[t]];
+    const float c = cos_t[(size_t) pos * 32 + i], s = sin_t[(size_t) pos * 32 + i];
+    const float * xr = x + (size_t) t * ldx;
+    const float qa0 = q_alpha[i], qa1 = q_alpha[32 + i], qb0 = q_beta[i], qb1 = q_beta[32 + i];
+    const float ka0 = k_alpha[i], ka1 = k_alpha[32 + i], kb0 = k_beta[i], kb1 = k_beta[32 + i];
+#pragma unroll 4
+    for (int h = 0; h < H; ++h) {
+        const float x1 = xr[64 * h + i], x2 = xr[64 * h + 32 + i];
+        const float a = __fmul_rn(qb0, tanh8(__fmul_rn(qa0, x1)));
+        const float b = __fmul_rn(qb1, tanh8(__fmul_rn(qa1, x2)));
+        float * y = q + ((size_t) t * H + h) * 64;
+        y[i] = __fmaf_rn(a, c, __fmul_rn(b, s));
+        y[32 + i] = __fmaf_rn(-a, s, __fmul_rn(b, c));
+    }
+    const float * xk = xr + 64 * H;
+#pragma unroll 4
+    for (int g = 0; g < G; ++g) {
+        const float x1 = xk[64 * g + i], x2 = xk[64 * g + 32 + i];
+        const float a = __fmul_rn(kb0, tanh8(__fmul_rn(ka0, x1)));
+        const float b = __fmul_rn(kb1, tanh8(__fmul_rn(ka1, x2)));
+        float * y = k + ((size_t) g * T + t) * 64;
+        y[i] = __fmaf_rn(a, c, __fmul_rn(b, s));
+        y[32 + i] = __fmaf_rn(-a, s, __fmul_rn(b, c));
+    }
+    const float * xv = xk + 64 * G;
+#pragma unroll 4
+    for (int g = 0; g < G; ++g) {
+        float * y = v + ((size_t) g * T + t) * 64;
+        y[i] = xv[64 * g + i];
+        y[32 + i] = xv[64 * g + 32 + i];
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -415,49 +556,47 @@ int32_t nxk_take_error(void * stream) {
 }
 
 int nxk_quantize(const float * x, int T, int C, int8_t * q, float * sx, void * stream) {
-    return launch_rows(CopyOp{x}, T, C, nullptr, q, sx, S(stream));
+    return launch_rows8(CopyOp{x}, T, C, nullptr, q, sx, S(stream));
 }
 
 int nxk_rms_norm(const float * x, const float * gain, float eps, int T, int C, float * out, int8_t * q, float * sx,
                  void * stream) {
-    return launch_rows(RmsOp{x, gain, eps, 0.0f}, T, C, out, q, sx, S(stream));
+    return launch_rows8(RmsOp{x, gain, eps, 0.0f}, T, C, out, q, sx, S(stream));
 }
 
 int nxk_relu_sqr(const float * x, int T, int C, float * out, int8_t * q, float * sx, void * stream) {
-    return launch_rows(ReluSqrOp{x}, T, C, out, q, sx, S(stream));
+    return launch_rows8(ReluSqrOp{x}, T, C, out, q, sx, S(stream));
 }
 
 int nxk_gate(const float * g, const float * y, int T, int C, float * out, int8_t * q, float * sx, void * stream) {
-    return launch_rows(GateOp{g, y}, T, C, out, q, sx, S(stream));
+    return launch_rows8(GateOp{g, y}, T, C, out, q, sx, S(stream));
 }
 
 int nxk_dwconv(const float * x, const float * r, const float * taps, int k, const int32_t * row_doc,
                const int32_t * doc_start, const int32_t * doc_len, int T, int C, float * out, int8_t * q,
                float * sx, void * stream) {
-    if (k <= 0) return NXK_EINVAL;
-    return launch_rows(DwconvOp{x, r, taps, k, row_doc, doc_start, doc_len, 0, 0}, T, C, out, q, sx, S(stream));
+    return launch_conv(false, x, nullptr, r, nullptr, taps, k, row_doc, doc_start, doc_len, T, C, out, q, sx, S(stream));
 }
 
 int nxk_lily_state(const float * a, const float * x, const float * b, const float * taps, int k,
                    const int32_t * row_doc, const int32_t * doc_start, const int32_t * doc_len, int T, int C,
                    float * out, int8_t * q, float * sx, void * stream) {
-    if (k <= 0) return NXK_EINVAL;
-    return launch_rows(LilyOp{a, x, b, taps, k, row_doc, doc_start, doc_len, 0, 0}, T, C, out, q, sx, S(stream));
+    return launch_conv(true, x, a, nullptr, b, taps, k, row_doc, doc_start, doc_len, T, C, out, q, sx, S(stream));
 }
 
 int nxk_block_mean(const float * h, const float * g, int C, int block, const int32_t * doc_start,
                    const int32_t * doc_len, const int32_t * bdoc_start, const int32_t * brow_doc, int n_brows,
                    float * out, int8_t * q, float * sx, void * stream) {
     if (block <= 0) return NXK_EINVAL;
-    return launch_rows(BlockMeanOp{h, g, block, doc_start, doc_len, bdoc_start, brow_doc, 0, 0, 0.0f},
-                       n_brows, C, out, q, sx, S(stream));
+    return launch_rows8(BlockMeanOp{h, g, block, doc_start, doc_len, bdoc_start, brow_doc, 0, 0, 0.0f},
+                        n_brows, C, out, q, sx, S(stream));
 }
 
 int nxk_upsample_add(const float * y, const float * r, int C, int block, int T, const int32_t * row_doc,
                      const int32_t * doc_start, const int32_t * bdoc_start, float * out, void * stream) {
     if (block <= 0) return NXK_EINVAL;
-    return launch_rows(UpsampleOp{y, r, block, row_doc, doc_start, bdoc_start, 0}, T, C, out, nullptr, nullptr,
-                       S(stream));
+    return launch_rows8(UpsampleOp{y, r, block, row_doc, doc_start, bdoc_start, 0}, T, C, out, nullptr, nullptr,
+                        S(stream));
 }
 
 int nxk_qk_prep(const float * x, const float * alpha, const float * beta, const float * cos_t, const float * sin_t,
@@ -468,6 +607,17 @@ int nxk_qk_prep(const float * x, const float * alpha, const float * beta, const 
     const size_t warps = (size_t) T * H;
     qk_prep_kernel<<<(unsigned) ((warps * 32 + 255) / 256), 256, 0, S(stream)>>>(
         x, alpha, beta, cos_t, sin_t, row_doc, doc_start, T, H, D, head_major, out);
+    return launched();
+}
+
+int nxk_qkv_prep(const float * x, int ldx, const float * q_alpha, const float * q_beta, const float * k_alpha,
+                 const float * k_beta, const float * cos_t, const float * sin_t, const int32_t * row_doc,
+                 const int32_t * doc_start, int T, int H, int G, int D, float * q, float * k, float * v,
+                 void * stream) {
+    if (T < 0 || H <= 0 || G <= 0 || D != 64 || ldx < (H + 2 * G) * D || (ldx & 3)) return NXK_EINVAL;
+    if (T == 0) return NXK_OK;
+    qkv_prep_kernel<<<(unsigned) (((size_t) T * 32 + 255) / 256), 256, 0, S(stream)>>>(
+        x, ldx, q_alpha, q_beta, k_alpha, k_beta, cos_t, sin_t, row_doc, doc_start, T, H, G, q, k, v);
     return launched();
 }
 

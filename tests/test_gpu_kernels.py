@@ -97,9 +97,11 @@ def test_linear_shapes(ops, oracle, T, K, N):
     assert np.array_equal(ops.linear(xq, xs, w8, sw, res), want)
 
 
-def test_quantize_and_row_ops_bit_exact(ops, oracle):
+@pytest.mark.parametrize("C", [512, 352])
+def test_quantize_and_row_ops_bit_exact(ops, oracle, C):
+    """C = 352: a partial last 256-column block"""
     from gpulib import P, dev
-    xr = cases.rows_case()
+    xr = cases.rows_case(C=C)
     T, C = xr.shape
     gain = (1.0 + 0.05 * np.random.default_rng(5).standard_normal(C)).astype(np.float32)
     qq, ss = ops.quant_out(T, C)
@@ -120,7 +122,7 @@ def test_quantize_and_row_ops_bit_exact(ops, oracle):
     wq, ws = oracle.quantize_rows(want)
     assert np.array_equal(q, wq) and np.array_equal(s, ws)
 
-    g = cases.rows_case(seed=9)
+    g = cases.rows_case(C=C, seed=9)
     want = oracle.gate(g, xr)
     assert np.array_equal(ops.rows("nxk_gate", [P(dev(g)), P(dev(xr)), T, C], T, C, False), want)
     q, s = ops.rows("nxk_gate", [P(dev(g)), P(dev(xr)), T, C], T, C, True)
@@ -163,6 +165,32 @@ def test_qk_prep_and_head_major_bit_exact(ops, oracle):
     out = torch.empty((4, T, 64), dtype=torch.float32, device="cuda")
     ops._ok(ops.L.nxk_head_major(P(dev(x)), T, 4, 64, P(out), None), "head_major")
     assert np.array_equal(host(out), oracle.head_major(x, 4, 64))
+
+
+def test_qkv_prep_bit_exact(ops, oracle):
+    """the fused q/k/v pass equals qk_prep (q token-major, k head-major) and head_major on the split columns"""
+    import torch
+    from gpulib import P, dev, host
+    L = cases.LENGTHS_SMALL
+    T = int(L.sum())
+    H, G, D = 4, 2, 64
+    rng = np.random.default_rng(77)
+    x = rng.standard_normal((T, (H + 2 * G) * D)).astype(np.float32)
+    qa, qb, ka, kb = (rng.uniform(0.2, 1.5, D).astype(np.float32) for _ in range(4))
+    start, ln, rd = ops.layout(L)
+    base = 10000.0
+    c, s = oracle.rope_table(int(L.max()), base, D)
+    q = torch.empty((T, H * D), dtype=torch.float32, device="cuda")
+    k = torch.empty((G, T, D), dtype=torch.float32, device="cuda")
+    v = torch.empty((G, T, D), dtype=torch.float32, device="cuda")
+    ops._ok(ops.L.nxk_qkv_prep(P(dev(x)), x.shape[1], P(dev(qa)), P(dev(qb)), P(dev(ka)), P(dev(kb)), P(dev(c)),
+                               P(dev(s)), P(dev(rd)), P(dev(start)), T, H, G, D, P(q), P(k), P(v), None), "qkv_prep")
+    xq = np.ascontiguousarray(x[:, :H * D])
+    xk = np.ascontiguousarray(x[:, H * D:(H + G) * D])
+    xv = np.ascontiguousarray(x[:, (H + G) * D:])
+    assert np.array_equal(host(q), oracle.qk_prep(xq, qa, qb, base, L, H, D, 0))
+    assert np.array_equal(host(k), oracle.qk_prep(xk, ka, kb, base, L, G, D, 1))
+    assert np.array_equal(host(v), oracle.head_major(xv, G, D))
 
 
 def test_hra_ops_bit_exact(ops, oracle):
