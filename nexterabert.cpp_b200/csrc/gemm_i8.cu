@@ -12,7 +12,10 @@
 // Kernel shape (one CTA per SM, persistent over 128x128 output tiles, tile
 // index n-fastest so the CTAs in flight share their activation tiles in L2):
 //   warp 0      TMA producer: 128x128-byte tiles of xq and w8 (SWIZZLE_128B)
-//               into a 4-stage shared-memory ring
+//               into a 4-stage shared-memory ring, and per tile the scales the
+//               epilogue needs (sw of its 128 columns, sx of its 128 rows) by
+//               bulk copy into a 2-slot ring, so the epilogue never waits on a
+//               global load
 //   warp 1      allocates TMEM (2 x 128 columns) and issues tcgen05.mma from one
 //               thread: 4 MMAs (K = 32 each) per 128-byte stage, one TMEM
 //               accumulator per 256-input block, alternating between the two
@@ -46,9 +49,10 @@ constexpr int THREADS = 32 * (2 + EPI_WARPS);
 constexpr int ACC = 4;                              // TMEM accumulators (one per 256-input block in flight)
 constexpr int TMEM_COLS = ACC * BN;                 // all 512 columns
 constexpr int MAX_BLK = 12;                         // K <= 3072
-constexpr int SW_BYTES = EPI_WARPS * MAX_BLK * 64 * 4;   // each epilogue warp's 64 columns of weight scales
+constexpr int SCALE_FLOATS = 2 * MAX_BLK * BN;           // one slot: sw [block][128 cols], sx [128 rows][block]
+constexpr int SCALE_BYTES = 2 * SCALE_FLOATS * 4;        // two slots
 constexpr int OUT_BYTES = EPI_WARPS * 32 * 64 * 4;       // each epilogue warp's 32 x 64 output slice (2 swizzled boxes)
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + SW_BYTES + 1024 /* alignment */ + 256 /* barriers */;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + SCALE_BYTES + 1024 /* alignment */ + 256 /* barriers */;
 constexpr uint32_t IDESC = idesc_i8(BM, BN);
 
 enum : int { ERR_PRODUCER = 0x101, ERR_MMA = 0x102, ERR_EPILOGUE = 0x103 };
@@ -70,10 +74,11 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
     uint8_t * sA = smem;
     uint8_t * sB = smem + STAGES * A_BYTES;
     float * so = (float *) (sB + STAGES * B_BYTES);                   // [EPI_WARPS][2][32 rows][32 floats], 1024-aligned
-    float * sw_s = (float *) ((uint8_t *) so + OUT_BYTES);            // [EPI_WARPS][MAX_BLK][64]
-    uint64_t * bars = (uint64_t *) ((uint8_t *) sw_s + SW_BYTES);
+    float * scl = (float *) ((uint8_t *) so + OUT_BYTES);             // [2][SCALE_FLOATS]
+    uint64_t * bars = (uint64_t *) ((uint8_t *) scl + SCALE_BYTES);
     uint64_t * full = bars, * empty = bars + STAGES, * accf = bars + 2 * STAGES, * acce = bars + 2 * STAGES + ACC;
-    uint32_t * tmem_slot = (uint32_t *) (bars + 2 * STAGES + 2 * ACC);
+    uint64_t * sfull = bars + 2 * STAGES + 2 * ACC, * sempty = sfull + 2;
+    uint32_t * tmem_slot = (uint32_t *) (sempty + 2);
     volatile int * abort_flag = (volatile int *) (tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -85,6 +90,10 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
         for (int b = 0; b < ACC; ++b) {
             mbar_init(smem_u32(&accf[b]), 1);
             mbar_init(smem_u32(&acce[b]), EPI_WARPS);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(smem_u32(&sfull[b]), 1);
+            mbar_init(smem_u32(&sempty[b]), EPI_WARPS);
         }
         *abort_flag = 0;
         fence_barrier_init();
@@ -104,10 +113,29 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
-            uint32_t it = 0;
+            uint32_t it = 0, tc = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
+            for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x, ++tc) {
                 const int m0 = (tile / a.tiles_n) * BM, n0 = (tile % a.tiles_n) * BN;
+                {
+                    // the tile's scales -> slot tc % 2: sw rows [block][n0, n0 + cols), sx rows [m0, m0 + rows)
+                    const uint32_t sb = tc & 1, su = tc >> 1;
+                    if (su > 0 && !mbar_wait(smem_u32(&sempty[sb]), (su - 1) & 1)) { ok = false; break; }
+                    if (*abort_flag) { ok = false; break; }
+                    float * slot = scl + sb * SCALE_FLOATS;
+                    float * sxs = slot + MAX_BLK * BN;
+                    const uint32_t cols = (uint32_t) min(BN, a.N - n0);
+                    const uint32_t sx_bytes = (uint32_t) min(BM, a.T - m0) * a.n_blk * 4;
+                    const uint32_t sx_bulk = sx_bytes & ~15u;
+                    const float * sxg = a.sx + (size_t) m0 * a.n_blk;
+                    for (uint32_t i = sx_bulk / 4; i < sx_bytes / 4; ++i) sxs[i] = sxg[i];   // tail: < 4 floats
+                    fence_proxy_async_smem();
+                    const uint32_t fb = smem_u32(&sfull[sb]);
+                    mbar_arrive_expect_tx(fb, (uint32_t) a.n_blk * cols * 4 + sx_bulk);
+                    for (int b = 0; b < a.n_blk; ++b)
+                        bulk_g2s(smem_u32(slot + b * BN), a.sw + (size_t) b * a.N + n0, cols * 4, fb);
+                    if (sx_bulk) bulk_g2s(smem_u32(sxs), sxg, sx_bulk, fb);
+                }
                 for (int c = 0; c < a.n_chunks; ++c, ++it) {
                     const uint32_t s = it % STAGES, u = it / STAGES;
                     if (u > 0 && !mbar_wait(smem_u32(&empty[s]), (u - 1) & 1)) { ok = false; break; }
@@ -125,6 +153,8 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
             // every issued copy lands before the CTA may exit
             const uint32_t first = it > STAGES ? it - STAGES : 0;
             for (uint32_t k = first; k < it; ++k) mbar_wait(smem_u32(&full[k % STAGES]), (k / STAGES) & 1);
+            const uint32_t sfirst = tc > 2 ? tc - 2 : 0;
+            for (uint32_t k = sfirst; k < tc; ++k) mbar_wait(smem_u32(&sfull[k & 1]), (k >> 1) & 1);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
@@ -166,20 +196,19 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
         // ------------------------------------------------------------ epilogue
         const int quad = warp & 3, halfc = (warp - 2) >> 2;
         const int row = 32 * quad + lane;
-        // this warp's private copy of its 64 columns' weight scales: only __syncwarp
-        // orders it, so no cross-warp barrier (which could not time out) is needed
-        float * sws = sw_s + (warp - 2) * MAX_BLK * 64;
-        uint32_t kb = 0;
+        uint32_t kb = 0, tc = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
+        for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x, ++tc) {
             const int m0 = (tile / a.tiles_n) * BM, n0 = (tile % a.tiles_n) * BN;
             const int t = m0 + row;
             const int nc = n0 + 64 * halfc;
-            __syncwarp();
-            if (nc < a.N) {
-                for (int i = lane; i < a.n_blk * 64; i += 32) sws[i] = a.sw[(size_t) (i >> 6) * a.N + nc + (i & 63)];
+            const uint32_t sb = tc & 1;
+            {
+                const bool got = mbar_wait(smem_u32(&sfull[sb]), (tc >> 1) & 1) && !*abort_flag;
+                if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
             }
-            __syncwarp();
+            const float * sws = scl + sb * SCALE_FLOATS + 64 * halfc;      // [block][128 cols], this warp's 64
+            const float * sxs = scl + sb * SCALE_FLOATS + MAX_BLK * BN;    // [128 rows][block]
             float2 f[32];
 #pragma unroll
             for (int c = 0; c < 32; ++c) f[c] = make_float2(0.0f, 0.0f);
@@ -197,10 +226,10 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
                 __syncwarp();
                 if (lane == 0) mbar_arrive(smem_u32(&acce[acc]));
                 if (nc >= a.N) continue;                                   // columns past N (N % 64 == 0)
-                const float sxb = t < a.T ? a.sx[(size_t) t * a.n_blk + b] : 0.0f;
+                const float sxb = t < a.T ? sxs[row * a.n_blk + b] : 0.0f;
                 const float2 sx2 = make_float2(sxb, sxb);
                 const float2 nmagic = make_float2(-12582912.0f, -12582912.0f);   // x - m == x + (-m) exactly
-                const float4 * swp = (const float4 *) (sws + b * 64);
+                const float4 * swp = (const float4 *) (sws + b * BN);
                 // f = fma(float(S) * sx, sw, f) per column, two columns per packed instruction;
                 // float(S) exact via the 1.5 * 2^23 bias (|S| <= 2^22)
 #pragma unroll
@@ -225,6 +254,8 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
                 }
             }
             if (!ok) break;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&sempty[sb]));             // scales slot free
             if (nc < a.N) {
                 // this warp's 32 x 64 slice -> shared memory (two 32 x 32 boxes in the 128-byte
                 // swizzle: 16-byte chunk c of row r at chunk c ^ (r % 8)) -> one TMA store or
@@ -351,6 +382,7 @@ int nxk_linear_i8(const int8_t * xq, const float * sx, int T, const int8_t * w8,
     if (T < 0 || K <= 0 || N <= 0 || (K & 31) || (N & 63) || !xq || !w8 || !sx || !sw || !out) return NXK_EINVAL;
     if ((K + I8_BLOCK - 1) / I8_BLOCK > MAX_BLK) return NXK_EINVAL;
     if (((uintptr_t) xq & 15) || ((uintptr_t) w8 & 15) || ((uintptr_t) out & 15)) return NXK_EINVAL;
+    if (((uintptr_t) sx & 15) || ((uintptr_t) sw & 15)) return NXK_EINVAL;     // bulk-copied scales
     if (res && ((uintptr_t) res & 15)) return NXK_EINVAL;
     if (T == 0) return NXK_OK;
     CUtensorMap ma, mb, mo;

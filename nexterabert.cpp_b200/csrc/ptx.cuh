@@ -74,6 +74,13 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void * tmap, int
         :: "r"(dst), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(bar) : "memory");
 }
 
+// contiguous global -> shared copy of `bytes` (a multiple of 16, both addresses 16-byte
+// aligned), completing on `bar` (no multicast)
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void * src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(dst), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar) : "memory");
+}
+
 // 2-D tiled store of one shared-memory box to global memory (bulk-group completion)
 __device__ __forceinline__ void tma_store_2d(const void * tmap, int32_t c0, int32_t c1, uint32_t src) {
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
