@@ -260,6 +260,28 @@ def int8_peak_tops(torch) -> float:
     return 2.0 * n ** 3 / (best * 1e-3) / 1e12
 
 
+def fp32_peak_tflops(torch) -> float:
+    """Measured fp32 FMA throughput: cuBLAS SGEMM with TF32 off (CUDA-core FFMA), 8192^3, TFLOP/s."""
+    n = 8192
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    a = torch.randn(n, n, device="cuda")
+    b = torch.randn(n, n, device="cuda")
+    for _ in range(2):
+        torch.matmul(a, b)
+    best = 1e30
+    for _ in range(5):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        torch.matmul(a, b)
+        e.record()
+        e.synchronize()
+        best = min(best, s.elapsed_time(e))
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    del a, b
+    return 2.0 * n ** 3 / (best * 1e-3) / 1e12
+
+
 def run_b200(args, rank, world, local_rank, dist):
     import torch
     from gpulib import load_lib
@@ -361,6 +383,8 @@ def run_b200(args, rank, world, local_rank, dist):
     except (OSError, ValueError):
         pass
     hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    hbm_src = ("MEASURED_PEAKS.json hbm_gbs (of measured)" if "hbm_gbs" in peaks
+               else "6650 GB/s, an earlier copy measurement on this pool (of fallback: MEASURED_PEAKS.json absent)")
     lin_ops = linear_ops(lengths)
     att_flops, att_bytes = attention_work(lengths)
     top = max(k_ms, key=k_ms.get)
@@ -372,22 +396,28 @@ def run_b200(args, rank, world, local_rank, dist):
                "peak_source": "dense int8 GEMM measured in this run (cuBLASLt via torch._int_mm, 8192^3, burst)",
                "algorithmic": "sum over the step's 141-per-token int8 linears of 2*T*N*K"}
         lin["frac"] = lin["achieved"] / lin["peak"]
-        att = {"bound": "hbm", "achieved": att_bytes / (k_ms["attention"] * 1e-3) / 1e9, "peak": hbm_peak,
-               "unit": "GB/s", "kernel": "attn_kernel (exact varlen GQA)",
-               "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)",
-               "algorithmic": "q + k + v read, output written once per attention layer (fp32)",
-               "fp32_tflops": att_flops / (k_ms["attention"] * 1e-3) / 1e12}
+        f32_peak = fp32_peak_tflops(torch)
+        # the attention's arithmetic is fixed fp32 fused multiply-add chains in the reference's
+        # order, which tensor cores cannot reproduce: its ceiling is the CUDA-core FMA pipe
+        att = {"bound": "fp32", "achieved": att_flops / (k_ms["attention"] * 1e-3) / 1e12, "peak": f32_peak,
+               "unit": "TFLOP/s", "kernel": "attn_tiled_kernel (exact varlen GQA)",
+               "peak_source": "fp32 FMA throughput measured in this run (cuBLAS SGEMM, TF32 off, 8192^3)",
+               "algorithmic": "2 * 64 multiply-adds per (query, head, key) for the scores and again for the "
+                              "weighted values, keys in each query's range",
+               "hbm_gbs": att_bytes / (k_ms["attention"] * 1e-3) / 1e9, "hbm_peak_gbs": hbm_peak,
+               "hbm_peak_source": hbm_src,
+               "hbm_algorithmic": "q + k + v read, output written once per attention layer (fp32)"}
         att["frac"] = att["achieved"] / att["peak"]
         roof = lin if top == "int8_linear" else att if top == "attention" else None
         if roof is None:
             roof = {"bound": "hbm", "achieved": None, "peak": hbm_peak, "unit": "GB/s", "frac": None,
-                    "kernel": "row ops"}
+                    "kernel": "row ops", "peak_source": hbm_src}
         tf = ROOT / "profiles" / "traffic.json"
         roof["traffic"] = None
         if tf.exists():
             try:
                 tr = json.loads(tf.read_text())
-                roof["traffic"] = tr.get(roof["kernel"].split()[0])
+                roof["traffic"] = tr.get(roof["kernel"].split()[0], {}).get("bytes_per_launch")
             except ValueError:
                 pass
         roof = dict(roof)
