@@ -78,6 +78,16 @@ NEXTERA_API int nxk_dwconv(const float * x, const float * r, const float * taps,
 NEXTERA_API int nxk_lily_state(const float * a, const float * x, const float * b, const float * taps, int k,
                                const int32_t * row_doc, const int32_t * doc_start, const int32_t * doc_len,
                                int T, int C, float * out, int8_t * q, float * sx, void * stream);
+/* The two token convolutions where the inputs x (and a) also hold halo rows: rows
+ * [-halo, T + halo) relative to the pointer may be read (those the documents reach); outputs
+ * are rows [0, T).  With halo = 0 these are nxk_dwconv / nxk_lily_state. */
+NEXTERA_API int nxk_dwconv_halo(const float * x, const float * r, const float * taps, int k, int halo,
+                                const int32_t * row_doc, const int32_t * doc_start, const int32_t * doc_len,
+                                int T, int C, float * out, int8_t * q, float * sx, void * stream);
+NEXTERA_API int nxk_lily_state_halo(const float * a, const float * x, const float * b, const float * taps, int k,
+                                    int halo, const int32_t * row_doc, const int32_t * doc_start,
+                                    const int32_t * doc_len, int T, int C, float * out, int8_t * q, float * sx,
+                                    void * stream);
 NEXTERA_API int nxk_qk_prep(const float * x, const float * alpha, const float * beta,
                             const float * cos_t, const float * sin_t, const int32_t * row_doc,
                             const int32_t * doc_start, int T, int H, int D, int head_major, float * out,
@@ -90,6 +100,13 @@ NEXTERA_API int nxk_qkv_prep(const float * x, int ldx, const float * q_alpha, co
                              const float * k_alpha, const float * k_beta, const float * cos_t,
                              const float * sin_t, const int32_t * row_doc, const int32_t * doc_start,
                              int T, int H, int G, int D, float * q, float * k, float * v, void * stream);
+/* nxk_qkv_prep writing k and v into buffers of Tk rows per head at rows koff .. koff + T - 1
+ * (the layout nxk_attention_kv reads). */
+NEXTERA_API int nxk_qkv_prep_kv(const float * x, int ldx, const float * q_alpha, const float * q_beta,
+                                const float * k_alpha, const float * k_beta, const float * cos_t,
+                                const float * sin_t, const int32_t * row_doc, const int32_t * doc_start,
+                                int T, int H, int G, int D, int Tk, int koff, float * q, float * k, float * v,
+                                void * stream);
 NEXTERA_API int nxk_block_mean(const float * h, const float * g, int C, int block,
                                const int32_t * doc_start, const int32_t * doc_len,
                                const int32_t * bdoc_start, const int32_t * brow_doc, int n_brows,
@@ -103,6 +120,11 @@ NEXTERA_API int nxk_layer_norm(const float * x, const float * w, const float * b
 /* run_forward's pooling (:1903-1918): per-document sum, then 1/n or 1/||sum|| */
 NEXTERA_API int nxk_pool(const float * hidden, const int32_t * doc_start, const int32_t * doc_len, int n_docs,
                          int C, int normalize, float * pooled, void * stream);
+/* The two halves of nxk_pool for a document split over several calls (shards in order):
+ * pooled[c] continues the sequential sum from its current value over hidden rows [0, T);
+ * nxk_pool_finish then applies 1/n (n = the whole length) or 1/||sum||. */
+NEXTERA_API int nxk_pool_continue(const float * hidden, int T, int C, float * pooled, void * stream);
+NEXTERA_API int nxk_pool_finish(int n, int C, int normalize, float * pooled, void * stream);
 
 /* ---- attention: op_attention (:785-852), varlen GQA over packed documents ----
  * half < 0: full attention inside each document, else the band |i - j| <= half.
@@ -115,6 +137,18 @@ NEXTERA_API int nxk_attention(const float * q, const float * k, const float * v,
                               const int32_t * doc_start, const int32_t * doc_len, int n_docs,
                               const int32_t * h_doc_start, const int32_t * h_doc_len,
                               void * workspace, size_t workspace_bytes, float * out, void * stream);
+
+/* nxk_attention with K / V in a buffer of Tk rows per head in which key row 0 (the row of query
+ * row 0) is row koff: a document's keys may then lie before or after the query rows, as for a
+ * shard of a long sequence whose K / V were gathered from all shards (Tk = total length, koff =
+ * the shard's offset) or extended by the neighbours' rows (a halo).  Documents are given relative
+ * to query row 0 and may start before it; only query rows [0, T) are computed.  Keys a tile needs
+ * outside [-koff, Tk - koff) give NXK_EINVAL. */
+NEXTERA_API int nxk_attention_kv(const float * q, const float * k, const float * v, int T, int Tk, int koff,
+                                 int H, int G, int D, int half, const float * scale,
+                                 const int32_t * doc_start, const int32_t * doc_len, int n_docs,
+                                 const int32_t * h_doc_start, const int32_t * h_doc_len,
+                                 void * workspace, size_t workspace_bytes, float * out, void * stream);
 
 /* nxk_attention without a workspace argument, for callers that cannot allocate
  * device memory when they call (a host that hands this library pointers into a

@@ -137,6 +137,28 @@ NEXTERA_API int32_t nextera_encode_device(struct nextera_context * ctx,
                                           float * d_hidden, float * d_pooled, int32_t normalize,
                                           void * stream);
 
+/* ---- one sequence split over several GPUs (one process per GPU) ----
+ * No counterpart in the reference, which runs on one host.  Each rank encodes a
+ * contiguous, equal part of the sequence; neighbours exchange the halo rows of the
+ * token convolutions and of the band-attention K / V, the full-attention layers
+ * gather every rank's K / V, and the pooled vector is summed rank after rank in the
+ * sequence's order, so every rank's rows and the pooled vector are the ones the whole
+ * sequence gives on one GPU.  Communication is NCCL (libnccl.so.2, loaded on first use). */
+
+/* Writes the 128-byte NCCL id for a new group; call on one rank and pass the bytes to all. */
+NEXTERA_API int32_t nextera_shard_unique_id(uint8_t * id);
+/* Joins the group (rank in [0, world)) on the context's device; every rank calls it with the
+ * same id.  Blocks until all ranks have joined.  0 on success. */
+NEXTERA_API int32_t nextera_shard_init(struct nextera_context * ctx, int32_t rank, int32_t world,
+                                       const uint8_t * id);
+/* Encodes this rank's n_local ids (device memory) of a sequence of n_total = world * n_local ids;
+ * n_local must be a multiple of the HRA block and at least the band half-width.  d_hidden
+ * ([n_local][n_embd], this rank's rows) and d_pooled ([n_embd], the whole sequence, on every rank)
+ * are device pointers, either may be NULL.  Enqueued on `stream`; every rank must call it. */
+NEXTERA_API int32_t nextera_encode_sharded(struct nextera_context * ctx, const int32_t * d_tokens, int32_t n_local,
+                                           int32_t n_total, float * d_hidden, float * d_pooled, int32_t normalize,
+                                           void * stream);
+
 #ifdef __cplusplus
 }
 #endif

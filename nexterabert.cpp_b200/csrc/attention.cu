@@ -276,8 +276,8 @@ __global__ void __launch_bounds__(128 * REP, 4 / REP)
 attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, const float * __restrict__ v,
                   float * __restrict__ out, const Item * __restrict__ items, int n_units, int G,
                   const float * __restrict__ scale, const int32_t * __restrict__ doc_start,
-                  const int32_t * __restrict__ doc_len, int T, int H, int half, float * __restrict__ scratch,
-                  int slot_keys) {
+                  const int32_t * __restrict__ doc_len, int T, int Tk, int koff, int H, int half,
+                  float * __restrict__ scratch, int slot_keys) {
     constexpr int NT = 128 * REP;
     constexpr int NQH = QT3 * REP;                                  // (query, head) pairs of a unit
     extern __shared__ __align__(16) float smem[];
@@ -304,8 +304,9 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
         const int g = u % G;
         const float sc = scale[it.doc];
         const int dlo = doc_start[it.doc], dhi = dlo + doc_len[it.doc];
-        const float * kg = k + (size_t) g * T * D;
-        const float * vg = v + (size_t) g * T * D;
+        // key row j (relative to query row 0, may be negative) of head g is at kg + j * D
+        const float * kg = k + ((ptrdiff_t) g * Tk + koff) * D;
+        const float * vg = v + ((ptrdiff_t) g * Tk + koff) * D;
         // the key range [lo, hi) of query row q0 + qi (empty past q1)
         auto range = [&](int qi, int & lo, int & hi) {
             const int t = it.q0 + qi;
@@ -351,7 +352,7 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
 #pragma unroll
             for (int z = 0; z < KPT; ++z) {
                 const int i = tid + z * NT, j = i % KT, d4 = i / KT;
-                kp[z] = kt + j < it.k1 ? *(const float4 *) (kg + (size_t) (kt + j) * D + 4 * d4)
+                kp[z] = kt + j < it.k1 ? *(const float4 *) (kg + (ptrdiff_t) (kt + j) * D + 4 * d4)
                                        : make_float4(0.f, 0.f, 0.f, 0.f);
             }
         };
@@ -439,7 +440,7 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
             if (p_sub == 0) {
                 // tail keys: hsum256 ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7)), then * scale
                 for (int kj = fe; kj < hi; ++kj) {
-                    const float4 * kr = (const float4 *) (kg + (size_t) kj * D);
+                    const float4 * kr = (const float4 *) (kg + (ptrdiff_t) kj * D);
                     float a8[8];
 #pragma unroll
                     for (int r = 0; r < 8; ++r) {
@@ -522,7 +523,7 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
 #pragma unroll
             for (int z = 0; z < VPT; ++z) {
                 const int i = tid + z * NT, j = i / (D / 4), d4 = i % (D / 4);
-                vp[z] = kt + j < it.k1 ? ((const float4 *) (vg + (size_t) (kt + j) * D))[d4]
+                vp[z] = kt + j < it.k1 ? ((const float4 *) (vg + (ptrdiff_t) (kt + j) * D))[d4]
                                        : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
@@ -577,12 +578,14 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
 }
 
 // one qt-query tile per item; key range = document, or the band around the tile
-void plan(const int32_t * start, const int32_t * len, int n_docs, int half, int qt, std::vector<Item> & items) {
+// Query rows are limited to [0, T): a document may reach outside them (a shard of a longer
+// sequence, whose keys lie in a gathered or halo-extended K / V).
+void plan(const int32_t * start, const int32_t * len, int n_docs, int half, int qt, int T, std::vector<Item> & items) {
     items.clear();
     for (int d = 0; d < n_docs; ++d) {
         const int lo = start[d], hi = lo + len[d];
-        for (int q0 = lo; q0 < hi; q0 += qt) {
-            const int q1 = std::min(hi, q0 + qt);
+        for (int q0 = std::max(lo, 0); q0 < std::min(hi, T); q0 += qt) {
+            const int q1 = std::min(std::min(hi, T), q0 + qt);
             Item it;
             it.q0 = q0;
             it.q1 = q1;
@@ -647,12 +650,27 @@ int nxk_attention(const float * q, const float * k, const float * v, int T, int 
                   const float * scale, const int32_t *, const int32_t * doc_start, const int32_t * doc_len,
                   int n_docs, const int32_t * h_doc_start, const int32_t * h_doc_len, void * workspace,
                   size_t workspace_bytes, float * out, void * stream) {
-    if (T < 0 || H <= 0 || G <= 0 || H % G || D != attn::D || n_docs < 0) return NXK_EINVAL;
+    return nxk_attention_kv(q, k, v, T, T, 0, H, G, D, half, scale, doc_start, doc_len, n_docs, h_doc_start,
+                            h_doc_len, workspace, workspace_bytes, out, stream);
+}
+
+int nxk_attention_kv(const float * q, const float * k, const float * v, int T, int Tk, int koff, int H, int G,
+                     int D, int half, const float * scale, const int32_t * doc_start, const int32_t * doc_len,
+                     int n_docs, const int32_t * h_doc_start, const int32_t * h_doc_len, void * workspace,
+                     size_t workspace_bytes, float * out, void * stream) {
+    if (T < 0 || Tk < 0 || koff < 0 || koff > Tk || H <= 0 || G <= 0 || H % G || D != attn::D || n_docs < 0)
+        return NXK_EINVAL;
+
     const int rep = H / G;
     if (rep != 1 && rep != 2 && rep != 4) return NXK_EINVAL;     // 64 * rep threads per block
     if (T == 0 || n_docs == 0) return NXK_OK;
     std::vector<attn::Item> items;
-    attn::plan(h_doc_start, h_doc_len, n_docs, half, attn::QT3, items);
+    attn::plan(h_doc_start, h_doc_len, n_docs, half, attn::QT3, T, items);
+    if (items.empty()) return NXK_OK;
+    // every key a tile touches must lie in [-koff, Tk - koff) relative to query row 0
+    for (const attn::Item & x : items) {
+        if (x.k0 < -koff || x.k1 > Tk - koff) return NXK_EINVAL;
+    }
     const attn::Scratch sp = attn::scratch_plan(h_doc_len, n_docs, half);
     const size_t item_bytes = (items.size() * sizeof(attn::Item) + 255) / 256 * 256;
     if (!workspace || workspace_bytes < item_bytes + sp.bytes) return NXK_EINVAL;
@@ -679,8 +697,8 @@ int nxk_attention(const float * q, const float * k, const float * v, int T, int 
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem_bytes);
         const long long resident = (long long) std::max(per_sm, 1) * std::max(sms, 1);
         const unsigned grid = (unsigned) std::min<long long>(std::min<long long>(n_units, sp.slots), resident);
-        kernel<<<grid, threads, smem_bytes, s>>>(q, k, v, out, it, (int) n_units, G, scale, doc_start, doc_len, T, H,
-                                                 half, scratch, sp.slot_keys);
+        kernel<<<grid, threads, smem_bytes, s>>>(q, k, v, out, it, (int) n_units, G, scale, doc_start, doc_len, T, Tk,
+                                                 koff, H, half, scratch, sp.slot_keys);
     };
     switch (rep) {
         case 1: launch(attn::attn_tiled_kernel<1>, 1); break;

@@ -17,6 +17,7 @@
 #include "nexterabert.h"
 #include "nextera_kernels.h"
 #include "gguf.hpp"
+#include "nccl_dl.hpp"
 
 #include <cuda_runtime.h>
 
@@ -39,6 +40,8 @@ enum cls_task { CLS_NONE, CLS_SEQUENCE, CLS_CHOICE, CLS_TOKEN, CLS_QA };
 const char * const CLS_NAMES[] = { "", "sequence-classification", "multiple-choice", "token-classification",
                                    "question-answering" };
 constexpr int I8_BLOCK = 256;
+// rows of padding before and after Fa / Fb / Fc: the halo a sharded token convolution reads
+constexpr int HALO_ROWS = 8;
 // the load-time concatenation of an attention mixer's c_q, c_k and c_v (no such tensor in a file)
 const char * const QKV_NAME = "c_qkv.weight#fused";
 
@@ -126,6 +129,11 @@ struct nextera_context {
     DevBuf rope_cos[2], rope_sin[2];
     int rope_n[2] = {0, 0};
     float rope_base_cached[2] = {0.0f, 0.0f};
+
+    // sequence sharding (nextera_shard_init): this process's rank, the ranks and their communicator
+    int shard_rank = 0, shard_world = 1;
+    ncclComm_t shard_comm = nullptr;
+    DevBuf kv_ext, kv_full;       // K / V with halo rows (band layers), gathered K / V (global, HRA)
 
     int32_t debug_n_layers = -1;
     profiler prof;
@@ -517,6 +525,7 @@ void nextera_free(struct nextera_context * c) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     for (auto & m : c->prof.marks) cudaEventDestroy(m.first);
     if (c->h_stage) cudaFreeHost(c->h_stage);
+    if (c->shard_comm) nxs::nccl().comm_destroy(c->shard_comm);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
 }
@@ -748,8 +757,9 @@ bool ensure_arena(nextera_context & c, const Batch & b) {
     const int64_t wide = std::max<int64_t>(I, 2 * (HD + 2 * GD));     // q, k, v and their fused projection
     const int64_t nb_C = (C + I8_BLOCK - 1) / I8_BLOCK, nb_W = (std::max(I, C) + I8_BLOCK - 1) / I8_BLOCK;
     bool ok = c.X.reserve(sizeof(float) * T * C) && c.X2.reserve(sizeof(float) * T * C) &&
-              c.U.reserve(sizeof(float) * T * wide) && c.Fa.reserve(sizeof(float) * T * C) &&
-              c.Fb.reserve(sizeof(float) * T * C) && c.Fc.reserve(sizeof(float) * T * C) &&
+              c.U.reserve(sizeof(float) * T * wide) && c.Fa.reserve(sizeof(float) * (T + 2 * HALO_ROWS) * C) &&
+              c.Fb.reserve(sizeof(float) * (T + 2 * HALO_ROWS) * C) &&
+              c.Fc.reserve(sizeof(float) * (T + 2 * HALO_ROWS) * C) &&
               c.Q1.reserve((size_t) T * std::max(I, C)) && c.Q1s.reserve(sizeof(float) * T * nb_W) &&
               c.Q2.reserve((size_t) T * C) && c.Q2s.reserve(sizeof(float) * T * nb_C);
     // staged metadata: row_doc T, brow_doc nb, start / len / bstart / blen per document, tokens T,
@@ -777,9 +787,35 @@ bool ensure_arena(nextera_context & c, const Batch & b) {
 }
 
 // One forward pass.  tokens / types are device pointers when the layout says so.
+// this rank's part of one sequence split over ranks (rows [offset, offset + Batch.T) of `total`)
+struct ShardRun {
+    int rank = 0, world = 1, offset = 0, total = 0;
+    ncclComm_t comm = nullptr;
+};
+
+// Fills rows [-h, 0) of x from the previous rank's last h rows and rows [rows, rows + h) from the
+// next rank's first h rows (x: rows of `width` floats).
+bool halo_rows(const ShardRun & sh, float * x, int rows, int width, int h, cudaStream_t s) {
+    if (h <= 0 || sh.world == 1) return true;
+    const nxs::NcclApi & n = nxs::nccl();
+    const size_t cnt = (size_t) h * width;
+    bool ok = nxs::nccl_ok(n.group_start(), "group start");
+    if (sh.rank > 0) {
+        ok = ok && nxs::nccl_ok(n.send(x, cnt, ncclFloat32, sh.rank - 1, sh.comm, s), "halo send");
+        ok = ok && nxs::nccl_ok(n.recv(x - cnt, cnt, ncclFloat32, sh.rank - 1, sh.comm, s), "halo recv");
+    }
+    if (sh.rank + 1 < sh.world) {
+        ok = ok && nxs::nccl_ok(n.send(x + (size_t) (rows - h) * width, cnt, ncclFloat32, sh.rank + 1, sh.comm, s),
+                                "halo send");
+        ok = ok && nxs::nccl_ok(n.recv(x + (size_t) rows * width, cnt, ncclFloat32, sh.rank + 1, sh.comm, s),
+                                "halo recv");
+    }
+    return nxs::nccl_ok(n.group_end(), "group end") && ok;
+}
+
 int run_encoder(nextera_context & c, const Batch & b, float rope0_base, const int32_t * tokens,
                 const int32_t * types, bool on_host, cudaStream_t s, float * d_hidden_out, float * d_pooled_out,
-                int normalize, float ** hidden_dev) {
+                int normalize, float ** hidden_dev, const ShardRun * sh = nullptr) {
     const hparams & hp = c.hp;
     const int T = b.T, C = hp.n_embd, H = hp.n_head, G = hp.n_kv_head, D = hp.head_dim;
     if (!ensure_arena(c, b) || !ensure_rope(c, 0, b.max_len, rope0_base) ||
@@ -838,7 +874,9 @@ int run_encoder(nextera_context & c, const Batch & b, float rope0_base, const in
     L.types = use_types ? (on_host ? dm + o_typ : types) : nullptr;
 
     float * X = c.X.as<float>(), * X2 = c.X2.as<float>(), * U = c.U.as<float>();
-    float * Fa = c.Fa.as<float>(), * Fb = c.Fb.as<float>(), * Fc = c.Fc.as<float>();
+    // row 0 of Fa / Fb / Fc comes after HALO_ROWS rows of padding (halo rows of a shard)
+    float * Fa = c.Fa.as<float>() + (size_t) HALO_ROWS * C, * Fb = c.Fb.as<float>() + (size_t) HALO_ROWS * C;
+    float * Fc = c.Fc.as<float>() + (size_t) HALO_ROWS * C;
     int8_t * Q1 = c.Q1.as<int8_t>(), * Q2 = c.Q2.as<int8_t>();
     float * Q1s = c.Q1s.as<float>(), * Q2s = c.Q2s.as<float>();
 
@@ -851,26 +889,69 @@ int run_encoder(nextera_context & c, const Batch & b, float rope0_base, const in
                           tt ? (int) tt->ne[1] : 0, L.types, X, s), "embed");
     }
 
-    // attention of a mixer over `rows` rows laid out by (start, len, row_doc)
+    // attention of a mixer over `rows` rows laid out by (start, len, row_doc).  Sharded, the keys
+    // come from beyond this rank's rows: band layers read `half` halo rows of the neighbours,
+    // full layers the K / V of all ranks, gathered (tot_rows rows, this rank's at row_off).
     auto attention = [&](const std::string & pre, const int8_t * hq, const float * hsx, int rows,
                          const int32_t * start, const int32_t * len, const int32_t * row_doc,
                          const std::vector<int32_t> & h_start, const std::vector<int32_t> & h_len, int rope,
-                         int half, const float * scale, float * y) {
-        float * q = U;
-        float * k = U + (size_t) rows * H * D;
-        float * v = k + (size_t) rows * G * D;
+                         int half, const float * scale, float * y, int tot_rows, int row_off) {
         // c_q, c_k, c_v as one GEMM over their concatenated rows (each output column is the
         // same dot product as in the separate layers), then DyT + RoPE and the layouts in one pass
         const int ld = (H + 2 * G) * D;
-        float * qkv = v + (size_t) rows * G * D;
+        float * q = U;
+        float * qkv = q + (size_t) rows * H * D;
+        float * k, * v;
+        int Tk, koff;
+        if (!sh) {
+            Tk = rows;
+            koff = 0;
+            k = qkv + (size_t) rows * ld;
+        } else if (half >= 0) {
+            Tk = rows + 2 * half;
+            koff = half;
+            k = c.kv_ext.as<float>();
+        } else {
+            Tk = tot_rows;
+            koff = row_off;
+            k = c.kv_full.as<float>();
+        }
+        v = k + (size_t) G * Tk * D;
         fw.linear(pre + QKV_NAME, hq, hsx, rows, nullptr, qkv);
         fw.mark(PROF_ROWS);
-        fw.rows(nxk_qkv_prep(qkv, ld, fw.p(pre + "q_norm.alpha"), fw.p(pre + "q_norm.beta"), fw.p(pre + "k_norm.alpha"),
-                             fw.p(pre + "k_norm.beta"), c.rope_cos[rope].as<float>(), c.rope_sin[rope].as<float>(),
-                             row_doc, start, rows, H, G, D, q, k, v, s), "qkv_prep");
+        fw.rows(nxk_qkv_prep_kv(qkv, ld, fw.p(pre + "q_norm.alpha"), fw.p(pre + "q_norm.beta"),
+                                fw.p(pre + "k_norm.alpha"), fw.p(pre + "k_norm.beta"), c.rope_cos[rope].as<float>(),
+                                c.rope_sin[rope].as<float>(), row_doc, start, rows, H, G, D, Tk, koff, q, k, v, s),
+                "qkv_prep");
         fw.mark(PROF_ATTN);
-        fw.rows(nxk_attention(q, k, v, rows, H, G, D, half, scale, row_doc, start, len, b.n_docs, h_start.data(),
-                              h_len.data(), c.attn_ws.p, c.attn_ws.bytes, y, s), "attention");
+        if (sh && fw.ok) {
+            const nxs::NcclApi & n = nxs::nccl();
+            bool ok = true;
+            if (half >= 0) {
+                for (int g = 0; ok && g < 2 * G; ++g)       // k heads, then v heads
+                    ok = halo_rows(*sh, k + ((size_t) g * Tk + koff) * D, rows, D, half, s);
+            } else {
+                // in place: head g's rows of this rank already sit at row_off of the gathered buffer
+                ok = nxs::nccl_ok(n.group_start(), "group start");
+                for (int g = 0; ok && g < 2 * G; ++g) {
+                    float * hb = k + (size_t) g * Tk * D;
+                    ok = nxs::nccl_ok(n.all_gather(hb + (size_t) koff * D, hb, (size_t) rows * D, ncclFloat32,
+                                                   sh->comm, s), "all-gather");
+                }
+                ok = nxs::nccl_ok(n.group_end(), "group end") && ok;
+            }
+            if (!ok) fw.ok = false;
+        }
+        fw.rows(nxk_attention_kv(q, k, v, rows, Tk, koff, H, G, D, half, scale, start, len, b.n_docs, h_start.data(),
+                                 h_len.data(), c.attn_ws.p, c.attn_ws.bytes, y, s), "attention");
+    };
+
+    // halo rows of a token convolution's input (sharded runs only); returns the halo to read
+    auto conv_halo = [&](float * x, int width, int k) {
+        if (!sh || !fw.ok) return 0;
+        const int h = k / 2;
+        if (!halo_rows(*sh, x, T, width, h, s)) fw.ok = false;
+        return h;
     };
 
     // x + c_proj(sigmoid(c_gate(y)) * z)  (gated_out, :1209-1214); y, z: [T][C]
@@ -895,22 +976,25 @@ int run_encoder(nextera_context & c, const Batch & b, float rope0_base, const in
             const ConvTaps * k1 = fw.taps(pre + "ltc_conv.kernel");
             if (!fw.ok) break;
             fw.mark(PROF_ROWS);
-            fw.rows(nxk_dwconv(Fa, Fb, k1->taps.as<float>(), k1->k, L.row_doc, L.start, L.len, T, r, nullptr, Q1, Q1s, s),
-                    "dwconv");
+            const int h1 = conv_halo(Fa, r, k1->k);
+            fw.rows(nxk_dwconv_halo(Fa, Fb, k1->taps.as<float>(), k1->k, h1, L.row_doc, L.start, L.len, T, r, nullptr,
+                                    Q1, Q1s, s), "dwconv");
             fw.linear(pre + "ltc_conv.out_proj.weight", Q1, Q1s, T, nullptr, Fa);
             fw.linear(pre + "x_proj.weight", Q2, Q2s, T, nullptr, Fb);
             fw.linear(pre + "B_proj.weight", Q2, Q2s, T, nullptr, Fc);
             const ConvTaps * k2 = fw.taps(pre + "state_conv.depthwise.weight");
             if (!fw.ok) break;
             fw.mark(PROF_ROWS);
-            fw.rows(nxk_lily_state(Fa, Fb, Fc, k2->taps.as<float>(), k2->k, L.row_doc, L.start, L.len, T, C, nullptr,
-                                   Q1, Q1s, s), "lily_state");
+            const int h2 = conv_halo(Fa, C, k2->k);
+            conv_halo(Fb, C, k2->k);
+            fw.rows(nxk_lily_state_halo(Fa, Fb, Fc, k2->taps.as<float>(), k2->k, h2, L.row_doc, L.start, L.len, T, C,
+                                        nullptr, Q1, Q1s, s), "lily_state");
             fw.linear(pre + "c_proj.weight", Q1, Q1s, T, X, X);      // x += c_proj(...), in place
         } else if (mt == MIX_SWA || mt == MIX_ATTN) {
             const bool swa = mt == MIX_SWA;
             const int half = swa ? std::max(1, hp.swa_window / 2) : -1;
             attention(pre, Q2, Q2s, T, L.start, L.len, L.row_doc, b.start, b.len, swa ? 1 : 0, half,
-                      d_scales + scale_off[l], Fb);
+                      d_scales + scale_off[l], Fb, sh ? sh->total : 0, sh ? sh->offset : 0);
             gated_out(pre, Fb, Fb, Fa);
         } else {
             // HRA (mix_hra, :1246-1264)
@@ -918,22 +1002,24 @@ int run_encoder(nextera_context & c, const Batch & b, float rope0_base, const in
             const ConvTaps * kq = fw.taps(pre + "qkv_conv.depthwise.weight");
             if (!fw.ok) break;
             fw.mark(PROF_ROWS);
-            fw.rows(nxk_dwconv(Fa, nullptr, kq->taps.as<float>(), kq->k, L.row_doc, L.start, L.len, T, C, Fb, nullptr,
-                               nullptr, s), "dwconv");
+            const int hq = conv_halo(Fa, C, kq->k);
+            fw.rows(nxk_dwconv_halo(Fa, nullptr, kq->taps.as<float>(), kq->k, hq, L.row_doc, L.start, L.len, T, C, Fb,
+                                    nullptr, nullptr, s), "dwconv");
             fw.linear(pre + "qkv_gate.weight", Q2, Q2s, T, nullptr, Fa);
             fw.mark(PROF_ROWS);
             fw.rows(nxk_block_mean(Fb, Fa, C, hp.hra_block, L.start, L.len, L.bstart, L.brow_doc, b.nb, nullptr, Q1, Q1s,
                                    s), "block_mean");
             attention(pre, Q1, Q1s, b.nb, L.bstart, L.blen, L.brow_doc, b.bstart, b.blen, 0, -1,
-                      d_scales + scale_off[l], Fa);
+                      d_scales + scale_off[l], Fa, sh ? sh->total / hp.hra_block : 0, sh ? sh->offset / hp.hra_block : 0);
             fw.linear(pre + "c_C.weight", Q2, Q2s, T, nullptr, Fb);
             fw.mark(PROF_ROWS);
             fw.rows(nxk_upsample_add(Fa, Fb, C, hp.hra_block, T, L.row_doc, L.start, L.bstart, Fc, s), "upsample_add");
             const ConvTaps * ko = fw.taps(pre + "c_o.depthwise.weight");
             if (!fw.ok) break;
             fw.mark(PROF_ROWS);
-            fw.rows(nxk_dwconv(Fc, nullptr, ko->taps.as<float>(), ko->k, L.row_doc, L.start, L.len, T, C, Fb, nullptr,
-                               nullptr, s), "dwconv");
+            const int ho = conv_halo(Fc, C, ko->k);
+            fw.rows(nxk_dwconv_halo(Fc, nullptr, ko->taps.as<float>(), ko->k, ho, L.row_doc, L.start, L.len, T, C, Fb,
+                                    nullptr, nullptr, s), "dwconv");
             gated_out(pre, Fc, Fb, Fa);
         }
         // MLP (:1284-1289)
@@ -954,7 +1040,23 @@ int run_encoder(nextera_context & c, const Batch & b, float rope0_base, const in
     }
     float * pooled = d_pooled_out ? d_pooled_out : c.pooled.as<float>();
     fw.mark(PROF_ROWS);
-    fw.rows(nxk_pool(hidden, L.start, L.len, b.n_docs, C, normalize, pooled, s), "pool", 2);
+    if (!sh) {
+        fw.rows(nxk_pool(hidden, L.start, L.len, b.n_docs, C, normalize, pooled, s), "pool", 2);
+    } else if (fw.ok) {
+        // the reference sums the sequence's rows in order: the running sum goes from rank to rank,
+        // each continuing it over its rows; the last rank scales it and sends it to all
+        const nxs::NcclApi & n = nxs::nccl();
+        bool ok = true;
+        if (sh->rank == 0) ok = cudaMemsetAsync(pooled, 0, sizeof(float) * C, s) == cudaSuccess;
+        else ok = nxs::nccl_ok(n.recv(pooled, C, ncclFloat32, sh->rank - 1, sh->comm, s), "pool recv");
+        if (ok) fw.rows(nxk_pool_continue(hidden, T, C, pooled, s), "pool");
+        if (ok && sh->rank + 1 < sh->world)
+            ok = nxs::nccl_ok(n.send(pooled, C, ncclFloat32, sh->rank + 1, sh->comm, s), "pool send");
+        if (ok && sh->rank + 1 == sh->world) fw.rows(nxk_pool_finish(sh->total, C, normalize, pooled, s), "pool");
+        if (ok)
+            ok = nxs::nccl_ok(n.broadcast(pooled, pooled, C, ncclFloat32, sh->world - 1, sh->comm, s), "broadcast");
+        if (!ok) fw.ok = false;
+    }
     if (d_hidden_out) cudaMemcpyAsync(d_hidden_out, hidden, sizeof(float) * (size_t) T * C, cudaMemcpyDeviceToDevice, s);
     fw.mark(-1);
     if (!fw.ok) return 3;
@@ -1032,6 +1134,94 @@ int32_t nextera_encode_device(struct nextera_context * c, const int32_t * d_toke
     float * hid = nullptr;
     return run_encoder(*c, b, rope0, d_tokens, d_token_types, false, (cudaStream_t) stream, d_hidden, d_pooled,
                        normalize, &hid);
+}
+
+int32_t nextera_shard_unique_id(uint8_t * id) {
+    if (!id) return 1;
+    const nxs::NcclApi & n = nxs::nccl();
+    if (!n.ok) return 3;
+    ncclUniqueId u;
+    if (!nxs::nccl_ok(n.get_unique_id(&u), "get unique id")) return 3;
+    memcpy(id, &u, sizeof(u));
+    return 0;
+}
+
+int32_t nextera_shard_init(struct nextera_context * c, int32_t rank, int32_t world, const uint8_t * id) {
+    if (!c || !id || world < 1 || rank < 0 || rank >= world) return 1;
+    const nxs::NcclApi & n = nxs::nccl();
+    if (!n.ok) return 3;
+    cudaSetDevice(c->device);
+    if (c->shard_comm) {
+        n.comm_destroy(c->shard_comm);
+        c->shard_comm = nullptr;
+    }
+    ncclUniqueId u;
+    memcpy(&u, id, sizeof(u));
+    if (!nxs::nccl_ok(n.comm_init_rank(&c->shard_comm, world, u, rank), "init")) {
+        c->shard_comm = nullptr;
+        return 3;
+    }
+    c->shard_rank = rank;
+    c->shard_world = world;
+    return 0;
+}
+
+int32_t nextera_encode_sharded(struct nextera_context * c, const int32_t * d_tokens, int32_t n_local, int32_t n_total,
+                               float * d_hidden, float * d_pooled, int32_t normalize, void * stream) {
+    if (!c || !d_tokens) return 1;
+    if (!c->shard_comm) {
+        fprintf(stderr, "nexterabert: nextera_encode_sharded before nextera_shard_init\n");
+        return 1;
+    }
+    const hparams & hp = c->hp;
+    const int world = c->shard_world, rank = c->shard_rank;
+    const int half = std::max(1, hp.swa_window / 2);
+    if (n_local <= 0 || (int64_t) n_local * world != n_total || n_local % hp.hra_block != 0 || n_local < half ||
+        n_local < HALO_ROWS) {
+        fprintf(stderr, "nexterabert: a sharded sequence needs n_total = %d x n_local, n_local a multiple of %d "
+                        "and at least %d (got n_local %d, n_total %d)\n",
+                world, hp.hra_block, std::max(half, HALO_ROWS), n_local, n_total);
+        return 1;
+    }
+    for (const auto & kv : c->taps) {
+        if (kv.second.k / 2 > HALO_ROWS) {
+            fprintf(stderr, "nexterabert: a convolution of %d taps is wider than the shard halo\n", kv.second.k);
+            return 1;
+        }
+    }
+    cudaSetDevice(c->device);
+    ShardRun sh;
+    sh.rank = rank;
+    sh.world = world;
+    sh.offset = rank * n_local;
+    sh.total = n_total;
+    sh.comm = c->shard_comm;
+    // one document relative to this rank's first row: [-offset, total - offset)
+    Batch b;
+    b.n_docs = 1;
+    b.T = n_local;
+    b.nb = n_local / hp.hra_block;
+    b.max_len = n_total;
+    b.start = {-sh.offset};
+    b.len = {n_total};
+    b.bstart = {-sh.offset / hp.hra_block};
+    b.blen = {n_total / hp.hra_block};
+    b.row_doc.assign(b.T, 0);
+    b.brow_doc.assign(b.nb, 0);
+    float rope0 = hp.rope_base;
+    if (hp.ntk_train_len > 0 && n_total > hp.ntk_train_len) {
+        const double d = hp.head_dim;
+        rope0 = (float) ((double) rope0 * std::pow((double) n_total / hp.ntk_train_len, d / (d - 2.0)));
+    }
+    const size_t G = hp.n_kv_head, D = hp.head_dim;
+    if (!c->kv_ext.reserve(sizeof(float) * 2 * G * (size_t) (n_local + 2 * half) * D) ||
+        !c->kv_full.reserve(sizeof(float) * 2 * G * (size_t) n_total * D)) {
+        fprintf(stderr, "nexterabert: failed to allocate the shard's K / V buffers\n");
+        return 2;
+    }
+    float * hid = nullptr;
+    return run_encoder(*c, b, rope0, d_tokens, nullptr, false, (cudaStream_t) stream, d_hidden, d_pooled, normalize,
+                       &hid, &sh);
 }
 
 int32_t nextera_pooler_output(struct nextera_context * c, const int32_t *, const int32_t *, const int32_t *, int32_t,

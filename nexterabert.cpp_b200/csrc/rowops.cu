@@ -224,7 +224,7 @@ inline size_t conv_smem_bytes(int k) { return sizeof(float) * 256 * (size_t) (CO
 template <bool LILY>
 __global__ void __launch_bounds__(256) conv_kernel(const float * __restrict__ x, const float * __restrict__ a,
                                                    const float * __restrict__ r, const float * __restrict__ b,
-                                                   const float * __restrict__ taps, int k,
+                                                   const float * __restrict__ taps, int k, int halo,
                                                    const int32_t * __restrict__ row_doc,
                                                    const int32_t * __restrict__ doc_start,
                                                    const int32_t * __restrict__ doc_len, int T, int C,
@@ -240,8 +240,8 @@ __global__ void __launch_bounds__(256) conv_kernel(const float * __restrict__ x,
     for (int i = threadIdx.x; i < n_rows * 64; i += blockDim.x) {
         const int rr = i >> 6, c4 = i & 63;
         const int tr = t0 - hk + rr;
-        if (tr < 0 || tr >= T || 4 * c4 >= ncol) continue;
-        const size_t off = (size_t) tr * C + cb + 4 * c4;
+        if (tr < -halo || tr >= T + halo || 4 * c4 >= ncol) continue;   // rows that exist
+        const ptrdiff_t off = (ptrdiff_t) tr * C + cb + 4 * c4;
         float4 xv = *(const float4 *) (x + off);
         if (LILY) {
             const float4 av = *(const float4 *) (a + off);
@@ -286,20 +286,21 @@ __global__ void __launch_bounds__(256) conv_kernel(const float * __restrict__ x,
 }
 
 int launch_conv(bool lily, const float * x, const float * a, const float * r, const float * b, const float * taps,
-                int k, const int32_t * row_doc, const int32_t * doc_start, const int32_t * doc_len, int T, int C,
-                float * out, int8_t * q, float * sx, cudaStream_t s) {
-    if (T < 0 || C <= 0 || (C & 31) || k <= 0 || k > CONV_KMAX || (!q && !out) || (q && !sx)) return NXK_EINVAL;
+                int k, int halo, const int32_t * row_doc, const int32_t * doc_start, const int32_t * doc_len, int T,
+                int C, float * out, int8_t * q, float * sx, cudaStream_t s) {
+    if (T < 0 || C <= 0 || (C & 31) || k <= 0 || k > CONV_KMAX || halo < 0 || (!q && !out) || (q && !sx))
+        return NXK_EINVAL;
     if (T == 0) return NXK_OK;
     const dim3 grid((unsigned) ((T + CONV_ROWS - 1) / CONV_ROWS), (unsigned) ((C + 255) / 256));
     const size_t smem = conv_smem_bytes(k);
     if (lily) {
         cudaFuncSetAttribute(conv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
-        conv_kernel<true><<<grid, 256, smem, s>>>(x, a, nullptr, b, taps, k, row_doc, doc_start, doc_len, T, C, out,
-                                                 q, sx);
+        conv_kernel<true><<<grid, 256, smem, s>>>(x, a, nullptr, b, taps, k, halo, row_doc, doc_start, doc_len, T, C,
+                                                 out, q, sx);
     } else {
         cudaFuncSetAttribute(conv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
-        conv_kernel<false><<<grid, 256, smem, s>>>(x, nullptr, r, nullptr, taps, k, row_doc, doc_start, doc_len, T, C,
-                                                  out, q, sx);
+        conv_kernel<false><<<grid, 256, smem, s>>>(x, nullptr, r, nullptr, taps, k, halo, row_doc, doc_start, doc_len,
+                                                  T, C, out, q, sx);
     }
     return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
 }
@@ -319,8 +320,8 @@ __global__ void __launch_bounds__(256) qkv_prep_kernel(const float * __restrict_
                                                        const float * __restrict__ sin_t,
                                                        const int32_t * __restrict__ row_doc,
                                                        const int32_t * __restrict__ doc_start, int T, int H, int G,
-                                                       float * __restrict__ q, float * __restrict__ k,
-                                                       float * __restrict__ v) {
+                                                       int Tk, int koff, float * __restrict__ q,
+                                                       float * __restrict__ k, float * __restrict__ v) {
     const int t = (int) ((blockIdx.x * (size_t) blockDim.x + threadIdx.x) >> 5);
     const int i = threadIdx.x & 31;
     if (t >= T) return;
@@ -344,14 +345,14 @@ __global__ void __launch_bounds__(256) qkv_prep_kernel(const float * __restrict_
         const float x1 = xk[64 * g + i], x2 = xk[64 * g + 32 + i];
         const float a = __fmul_rn(kb0, tanh8(__fmul_rn(ka0, x1)));
         const float b = __fmul_rn(kb1, tanh8(__fmul_rn(ka1, x2)));
-        float * y = k + ((size_t) g * T + t) * 64;
+        float * y = k + ((size_t) g * Tk + koff + t) * 64;
         y[i] = __fmaf_rn(a, c, __fmul_rn(b, s));
         y[32 + i] = __fmaf_rn(-a, s, __fmul_rn(b, c));
     }
     const float * xv = xk + 64 * G;
 #pragma unroll 4
     for (int g = 0; g < G; ++g) {
-        float * y = v + ((size_t) g * T + t) * 64;
+        float * y = v + ((size_t) g * Tk + koff + t) * 64;
         y[i] = xv[64 * g + i];
         y[32 + i] = xv[64 * g + 32 + i];
     }
@@ -451,13 +452,9 @@ __global__ void pool_sum_kernel(const float * __restrict__ hidden, const int32_t
     pooled[i] = s;
 }
 
-__global__ void pool_scale_kernel(const int32_t * __restrict__ doc_len, int n_docs, int C, int normalize,
-                                  float * __restrict__ pooled) {
-    const int d = (int) ((blockIdx.x * (size_t) blockDim.x + threadIdx.x) >> 5);
-    const int lane = threadIdx.x & 31;
-    if (d >= n_docs) return;
-    float * pv = pooled + (size_t) d * C;
-    float scale = __fdiv_rn(1.0f, (float) doc_len[d]);
+// 1/n, or 1/||sum|| when normalizing, applied to one pooled row by one warp
+__device__ __forceinline__ void pool_scale_row(float * pv, int n, int C, int normalize, int lane) {
+    float scale = __fdiv_rn(1.0f, (float) n);
     if (normalize) {
         float acc = 0.0f;
         for (int i = 0; i < (C >> 5); ++i) {
@@ -468,6 +465,37 @@ __global__ void pool_scale_kernel(const int32_t * __restrict__ doc_len, int n_do
         scale = nrm > 0.0f ? __fdiv_rn(1.0f, nrm) : 0.0f;
     }
     for (int c = lane; c < C; c += 32) pv[c] = __fmul_rn(pv[c], scale);
+}
+
+__global__ void pool_scale_kernel(const int32_t * __restrict__ doc_len, int n_docs, int C, int normalize,
+                                  float * __restrict__ pooled) {
+    const int d = (int) ((blockIdx.x * (size_t) blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
+    if (d >= n_docs) return;
+    pool_scale_row(pooled + (size_t) d * C, doc_len[d], C, normalize, lane);
+}
+
+// pooled[c] += hidden[t][c] for t = 0 .. T-1 in order (the continuation of pool_sum_kernel's sum)
+__global__ void pool_continue_kernel(const float * __restrict__ hidden, int T, int C, float * __restrict__ pooled) {
+    const int c = (int) (blockIdx.x * (size_t) blockDim.x + threadIdx.x);
+    if (c >= C) return;
+    const float * h = hidden + c;
+    float s = pooled[c];
+    int t = 0;
+    for (; t + 4 <= T; t += 4) {       // loads issued together, adds kept in order
+        const float a0 = h[(size_t) t * C], a1 = h[(size_t) (t + 1) * C];
+        const float a2 = h[(size_t) (t + 2) * C], a3 = h[(size_t) (t + 3) * C];
+        s = __fadd_rn(s, a0);
+        s = __fadd_rn(s, a1);
+        s = __fadd_rn(s, a2);
+        s = __fadd_rn(s, a3);
+    }
+    for (; t < T; ++t) s = __fadd_rn(s, h[(size_t) t * C]);
+    pooled[c] = s;
+}
+
+__global__ void pool_finish_kernel(int n, int C, int normalize, float * __restrict__ pooled) {
+    pool_scale_row(pooled, n, C, normalize, threadIdx.x & 31);
 }
 
 // ---------------------------------------------------------------------------
@@ -575,13 +603,28 @@ int nxk_gate(const float * g, const float * y, int T, int C, float * out, int8_t
 int nxk_dwconv(const float * x, const float * r, const float * taps, int k, const int32_t * row_doc,
                const int32_t * doc_start, const int32_t * doc_len, int T, int C, float * out, int8_t * q,
                float * sx, void * stream) {
-    return launch_conv(false, x, nullptr, r, nullptr, taps, k, row_doc, doc_start, doc_len, T, C, out, q, sx, S(stream));
+    return launch_conv(false, x, nullptr, r, nullptr, taps, k, 0, row_doc, doc_start, doc_len, T, C, out, q, sx,
+                       S(stream));
+}
+
+int nxk_dwconv_halo(const float * x, const float * r, const float * taps, int k, int halo, const int32_t * row_doc,
+                    const int32_t * doc_start, const int32_t * doc_len, int T, int C, float * out, int8_t * q,
+                    float * sx, void * stream) {
+    return launch_conv(false, x, nullptr, r, nullptr, taps, k, halo, row_doc, doc_start, doc_len, T, C, out, q, sx,
+                       S(stream));
 }
 
 int nxk_lily_state(const float * a, const float * x, const float * b, const float * taps, int k,
                    const int32_t * row_doc, const int32_t * doc_start, const int32_t * doc_len, int T, int C,
                    float * out, int8_t * q, float * sx, void * stream) {
-    return launch_conv(true, x, a, nullptr, b, taps, k, row_doc, doc_start, doc_len, T, C, out, q, sx, S(stream));
+    return launch_conv(true, x, a, nullptr, b, taps, k, 0, row_doc, doc_start, doc_len, T, C, out, q, sx, S(stream));
+}
+
+int nxk_lily_state_halo(const float * a, const float * x, const float * b, const float * taps, int k, int halo,
+                        const int32_t * row_doc, const int32_t * doc_start, const int32_t * doc_len, int T, int C,
+                        float * out, int8_t * q, float * sx, void * stream) {
+    return launch_conv(true, x, a, nullptr, b, taps, k, halo, row_doc, doc_start, doc_len, T, C, out, q, sx,
+                       S(stream));
 }
 
 int nxk_block_mean(const float * h, const float * g, int C, int block, const int32_t * doc_start,
@@ -614,10 +657,19 @@ int nxk_qkv_prep(const float * x, int ldx, const float * q_alpha, const float * 
                  const float * k_beta, const float * cos_t, const float * sin_t, const int32_t * row_doc,
                  const int32_t * doc_start, int T, int H, int G, int D, float * q, float * k, float * v,
                  void * stream) {
+    return nxk_qkv_prep_kv(x, ldx, q_alpha, q_beta, k_alpha, k_beta, cos_t, sin_t, row_doc, doc_start, T, H, G, D, T, 0,
+                           q, k, v, stream);
+}
+
+int nxk_qkv_prep_kv(const float * x, int ldx, const float * q_alpha, const float * q_beta, const float * k_alpha,
+                    const float * k_beta, const float * cos_t, const float * sin_t, const int32_t * row_doc,
+                    const int32_t * doc_start, int T, int H, int G, int D, int Tk, int koff, float * q, float * k,
+                    float * v, void * stream) {
     if (T < 0 || H <= 0 || G <= 0 || D != 64 || ldx < (H + 2 * G) * D || (ldx & 3)) return NXK_EINVAL;
+    if (koff < 0 || (long long) koff + T > Tk) return NXK_EINVAL;
     if (T == 0) return NXK_OK;
     qkv_prep_kernel<<<(unsigned) (((size_t) T * 32 + 255) / 256), 256, 0, S(stream)>>>(
-        x, ldx, q_alpha, q_beta, k_alpha, k_beta, cos_t, sin_t, row_doc, doc_start, T, H, G, q, k, v);
+        x, ldx, q_alpha, q_beta, k_alpha, k_beta, cos_t, sin_t, row_doc, doc_start, T, H, G, Tk, koff, q, k, v);
     return launched();
 }
 
@@ -644,6 +696,19 @@ int nxk_pool(const float * hidden, const int32_t * doc_start, const int32_t * do
     const size_t n = (size_t) n_docs * C;
     pool_sum_kernel<<<(unsigned) ((n + 255) / 256), 256, 0, S(stream)>>>(hidden, doc_start, doc_len, n_docs, C, pooled);
     pool_scale_kernel<<<(unsigned) ((n_docs + 7) / 8), 256, 0, S(stream)>>>(doc_len, n_docs, C, normalize, pooled);
+    return launched();
+}
+
+int nxk_pool_continue(const float * hidden, int T, int C, float * pooled, void * stream) {
+    if (T < 0 || C <= 0) return NXK_EINVAL;
+    if (T == 0) return NXK_OK;
+    pool_continue_kernel<<<(unsigned) ((C + 255) / 256), 256, 0, S(stream)>>>(hidden, T, C, pooled);
+    return launched();
+}
+
+int nxk_pool_finish(int n, int C, int normalize, float * pooled, void * stream) {
+    if (n <= 0 || C <= 0 || (C & 31)) return NXK_EINVAL;
+    pool_finish_kernel<<<1, 32, 0, S(stream)>>>(n, C, normalize, pooled);
     return launched();
 }
 

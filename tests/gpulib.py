@@ -84,11 +84,33 @@ def load_lib(path=None):
         "nextera_debug_launches": ([vp], ctypes.c_int64),
         "nextera_debug_profile_get": ([vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)],
                                       ctypes.c_int64),
+        "nextera_shard_unique_id": ([ctypes.c_char_p], ctypes.c_int32),
+        "nextera_shard_init": ([vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_char_p], ctypes.c_int32),
+        "nextera_encode_sharded": ([vp, vp, ctypes.c_int32, ctypes.c_int32, vp, vp, ctypes.c_int32, vp],
+                                   ctypes.c_int32),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
         fn.argtypes, fn.restype = args, res
     return L
+
+
+def shard_id(L, rank: int, dist=None) -> bytes:
+    """The 128-byte NCCL id of a sharded group: made by rank 0 through the library, handed to the
+    other ranks over `dist` (torch.distributed, any backend) when given."""
+    buf = ctypes.create_string_buffer(128)
+    if rank == 0:
+        rc = L.nextera_shard_unique_id(buf)
+        if rc != 0:
+            raise RuntimeError(f"nextera_shard_unique_id returned {rc}")
+    if dist is not None:
+        import torch
+        t = torch.frombuffer(bytearray(buf.raw), dtype=torch.uint8).clone()
+        if dist.get_backend() == "nccl":
+            t = t.cuda()
+        dist.broadcast(t, 0)
+        return bytes(t.cpu().numpy().tobytes())
+    return buf.raw
 
 
 # -- torch plumbing -------------------------------------------------------------

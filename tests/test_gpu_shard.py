@@ -1,0 +1,71 @@
+"""One sequence encoded by two GPUs (nextera_shard_init / nextera_encode_sharded).
+
+Each rank's rows of the last hidden state and the pooled vector must be bit-identical to the whole
+sequence encoded on one GPU: the token convolutions read their neighbours' halo rows, the band
+attention the neighbours' K / V rows, the full attention (and HRA) every rank's K / V, and the
+pooled sum runs over the ranks in the sequence's order.  Needs two GPUs; skipped otherwise.
+"""
+from __future__ import annotations
+
+import multiprocessing as mp
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+sys.path.insert(0, str(Path(__file__).resolve().parent / "golden"))
+import synth_model as sm  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def _two_gpus() -> bool:
+    try:
+        import torch
+        return torch.cuda.device_count() >= 2
+    except Exception:
+        return False
+
+
+def _run_two_ranks(model_path: Path, tokens: np.ndarray):
+    from gpulib import load_lib, shard_id
+    import shard_worker
+
+    L = load_lib()
+    nid = shard_id(L, 0)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=shard_worker.run, args=(r, 2, str(model_path), nid, tokens.tolist(), q))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    results = []
+    try:
+        for _ in range(2):
+            results.append(q.get(timeout=600))
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+                p.join()
+    return sorted(results)
+
+
+@pytest.mark.skipif(not _two_gpus(), reason="needs two GPUs")
+@pytest.mark.parametrize("which", ["tiny", "full"])
+def test_sharded_sequence_matches_one_gpu(which):
+    if which == "tiny":
+        path = sm.cached_model("tiny", sm.tiny_hparams(), "Q4_K_M", seed=0)
+        n, vocab = 512, 1000
+    else:
+        path = sm.cached_model("full", sm.full_hparams(), "Q4_K_M", seed=0)
+        n, vocab = 2048, 50368
+    tokens = sm.random_tokens(n, vocab, seed=11)
+    res = _run_two_ranks(path, tokens)
+    for r in res:
+        assert r[1] == "ok", r
+        rank, _, hid_eq, hid_diff, pool_eq, pool_diff = r
+        assert hid_eq, f"rank {rank}: hidden rows differ (max |diff| {hid_diff})"
+        assert pool_eq, f"rank {rank}: pooled differs (max |diff| {pool_diff})"

@@ -84,3 +84,44 @@ def test_kernel_layer_rejects_unsupported_shapes(built):
     assert L.nxk_rms_norm(None, None, 1e-8, 4, 100, None, None, None, None) == -1         # C not a multiple of 32
     assert L.nxk_attention(None, None, None, 4, 16, 2, 64, -1, None, None, None, None, 1, None, None,
                            None, 0, None, None) == -1                                     # 8 heads per KV head
+
+
+def test_shard_id_without_gpu():
+    """The NCCL id of a sharded group is made on the host (no GPU needed): 128 bytes, fresh each call."""
+    from gpulib import load_lib, shard_id
+    L = load_lib()
+    a, b = shard_id(L, 0), shard_id(L, 0)
+    assert len(a) == 128 and len(b) == 128 and a != b
+
+
+def _shard_id_rank(rank, port, q):
+    import os
+    import torch.distributed as dist
+    from gpulib import load_lib, shard_id
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    try:
+        q.put((rank, shard_id(load_lib(), rank, dist)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_shard_id_exchange_gloo():
+    """Two ranks (gloo, CPU): rank 0's id reaches rank 1 unchanged, as bench.py hands it out."""
+    import multiprocessing as mp
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_shard_id_rank, args=(r, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(2))
+    for p in ps:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert got[0] == got[1] and len(got[0]) == 128
