@@ -22,6 +22,10 @@ so the global batch grows with N ("scaling": "weak").
           on this host's cores over a bounded sample of the same batch (rank 0, N=1)
 
 --impl reference times only that CPU implementation (rank 0; other ranks exit).
+
+--config 5 [--seq-len 65536]: one long sequence instead (its own metric, strong scaling): one GPU
+encodes it whole; N ranks share it with nextera_encode_sharded (halo rows and K/V all-gather over
+NCCL), value = sequence tokens / step time, max over ranks.
 """
 from __future__ import annotations
 
@@ -221,6 +225,118 @@ def config(args, world, tokens_per_gpu):
             "global_batch": args.docs * world, "seq_len": "16-2048 (unpadded)",
             "parallelism": f"dp{world} (sequence-partitioned replicas)",
             "l2": "inputs larger than L2 (each activation tensor ~6.9 GB)"}
+
+
+LONG_METRIC = "encoded tokens/s (one 65,536-token sequence, Q4_K_M)"
+
+
+def run_long(args, rank, world, local_rank, dist):
+    """Config 5: one sequence of args.seq_len ids; N ranks share it (nextera_encode_sharded), so the
+    total work is fixed as N grows ("scaling": "strong")."""
+    import torch
+    import synth_model as sm
+    from gpulib import load_lib, shard_id
+
+    torch.cuda.set_device(local_rank)
+    dev_uuid = str(torch.cuda.get_device_properties(local_rank).uuid)
+    gpu_id = dev_uuid if dev_uuid.startswith("GPU-") else f"GPU-{dev_uuid}"
+    L = load_lib()
+    path = model_path(args.preset, rank, world, dist)
+    n_total = args.seq_len
+    if n_total % (4 * world):
+        raise SystemExit(f"--seq-len must be a multiple of 4 x {world}")
+    n_local = n_total // world
+    tokens = sm.random_tokens(n_total, 50368, seed=5)
+    h = L.nextera_load(str(path).encode(), L.nextera_default_params())
+    assert h, "nextera_load failed"
+    C = 1024
+    stream = torch.cuda.current_stream()
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+    local = np.ascontiguousarray(tokens[rank * n_local:(rank + 1) * n_local])
+    d_tok = torch.from_numpy(local).cuda()
+    d_pool = torch.empty(C, dtype=torch.float32, device="cuda")
+    lens = (ctypes.c_int32 * 1)(n_total)
+    if world > 1:
+        rc = L.nextera_shard_init(h, rank, world, shard_id(L, rank, dist))
+        assert rc == 0, f"nextera_shard_init returned {rc}"
+
+    def step(tok):
+        if world == 1:
+            rc = L.nextera_encode_device(h, ctypes.c_void_p(tok.data_ptr()), None, lens, 1, None,
+                                         ctypes.c_void_p(d_pool.data_ptr()), 1, sptr)
+        else:
+            rc = L.nextera_encode_sharded(h, ctypes.c_void_p(tok.data_ptr()), n_local, n_total, None,
+                                          ctypes.c_void_p(d_pool.data_ptr()), 1, sptr)
+        assert rc == 0, f"encode returned {rc}"
+
+    if args.profile_run:
+        step(d_tok)
+        torch.cuda.synchronize()
+        return
+    for _ in range(args.warmup):
+        step(d_tok)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(gpu_id)
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    l0 = L.nextera_debug_launches(h)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step(d_tok)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    launches = int(L.nextera_debug_launches(h) - l0)
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    value = n_total / (ms_step * 1e-3)
+
+    # e2e: this rank's ids from pinned host memory, the pooled vector back to the host, every step
+    h_tok = torch.from_numpy(local).pin_memory()
+    h_pool = torch.empty(C, dtype=torch.float32).pin_memory()
+    d_tok2 = torch.empty_like(d_tok)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        d_tok2.copy_(h_tok, non_blocking=True)
+        step(d_tok2)
+        h_pool.copy_(d_pool, non_blocking=True)
+        torch.cuda.synchronize()
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = {"value": n_total / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": int(4 * n_local),
+           "d2h_bytes_per_step": int(4 * C), "ms_per_step": 1000.0 * e2e_s,
+           "api": "nextera_encode_device / nextera_encode_sharded with pinned host copies in the timed loop"}
+    L.nextera_free(h)
+    log(f"rank {rank}: {ms_step:.1f} ms/step, {value:.0f} tokens/s, e2e {e2e['value']:.0f} tokens/s")
+    if rank == 0:
+        att_flops, _ = attention_work(np.array([n_total]))
+        line = {"metric": LONG_METRIC, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "int8+fp32", "data": "synthetic (seeded token ids; random-init weights N(0,0.02))",
+                "value": value, "ms_per_step": ms_step, "e2e": e2e, "clocks": clocks, "gpu_launches": launches,
+                "config": {"workload": f"cfg5: one sequence of {n_total} ids, {args.preset} random-init NexteraBERT "
+                                       "(18 layers, hidden 1024)",
+                           "seq_len": n_total, "tokens_per_gpu_step": n_local,
+                           "parallelism": f"sequence sharded over {world} GPU(s): halo rows and K/V all-gather "
+                                          "over NCCL" if world > 1 else "one GPU",
+                           "linear_int_ops_per_step": linear_ops(np.array([n_total])),
+                           "attention_flop_per_step": att_flops}}
+        print(json.dumps(line), flush=True)
 
 
 # ---------------------------------------------------------------- main
@@ -447,6 +563,9 @@ def main() -> int:
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--preset", default="Q4_K_M")
     ap.add_argument("--docs", type=int, default=4096)
+    ap.add_argument("--config", type=int, choices=[4, 5], default=4,
+                    help="4: mixed-length batch (the headline); 5: one long sequence, sharded over the GPUs")
+    ap.add_argument("--seq-len", type=int, default=65536, help="config 5 sequence length")
     ap.add_argument("--profile-run", action="store_true", help="one untimed step (for profilers)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -463,9 +582,13 @@ def main() -> int:
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device(f"cuda:{local_rank}"))
     try:
-        run_b200(args, rank, world, local_rank, dist)
+        if args.config == 5:
+            run_long(args, rank, world, local_rank, dist)
+        else:
+            run_b200(args, rank, world, local_rank, dist)
     finally:
         if dist is not None:
             dist.destroy_process_group()

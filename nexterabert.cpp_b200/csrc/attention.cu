@@ -608,9 +608,9 @@ size_t n_items(const int32_t * len, int n_docs, int qt) {
 // Score scratch of the tiled kernel: one slot per resident CTA, each holding
 // (longest key range) x (query, head) floats, sized for 4 query heads per KV
 // head (the most this build runs).  Slots: 4 per SM, at least one per SM,
-// and no more than fit in 8 GiB.
+// and no more than fit in 24 GiB (a 65,536-key range needs 64 MiB per slot).
 constexpr int SLOTS_PER_SM = 4;
-constexpr size_t SCRATCH_BUDGET = (size_t) 8 << 30;
+constexpr size_t SCRATCH_BUDGET = (size_t) 24 << 30;
 
 struct Scratch {
     int slot_keys = 0;
