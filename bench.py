@@ -52,6 +52,18 @@ def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
 
+# The result line is the only thing this program writes to its standard output.  Libraries
+# print there too (NCCL announces its version at initialisation when NCCL_DEBUG asks for it),
+# so main() points file descriptor 1 at standard error and keeps a copy of the original for emit().
+_RESULT_OUT = None
+
+
+def emit(line: dict) -> None:
+    out = _RESULT_OUT if _RESULT_OUT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 # ---------------------------------------------------------------- workload
 def workload(rank: int, n_docs: int):
     import synth_model as sm
@@ -336,7 +348,7 @@ def run_long(args, rank, world, local_rank, dist):
                                           "over NCCL" if world > 1 else "one GPU",
                            "linear_int_ops_per_step": linear_ops(np.array([n_total])),
                            "attention_flop_per_step": att_flops}}
-        print(json.dumps(line), flush=True)
+        emit(line)
 
 
 # ---------------------------------------------------------------- main
@@ -354,7 +366,7 @@ def run_reference(args, rank, world, dist):
                  "config": config(args, world, int(lengths.sum())),
                  "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": kind, "sample": sample},
                  "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def int8_peak_tops(torch) -> float:
@@ -552,10 +564,14 @@ def run_b200(args, rank, world, local_rank, dist):
         line.update({"value": value, "ms_per_step": ms_step, "config": config(args, world, T),
                      "e2e": e2e, "roofline": roof, "cpu_baseline": cpu, "clocks": clocks,
                      "gpu_launches": launches, "device_ms_by_kind": k_ms, "shares": shares})
-        print(json.dumps(line), flush=True)
+        emit(line)
 
 
 def main() -> int:
+    global _RESULT_OUT
+    sys.stdout.flush()
+    _RESULT_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
