@@ -266,6 +266,15 @@ attn_kernel(const float * __restrict__ q, const float * __restrict__ k, const fl
 // ---------------------------------------------------------------------------
 constexpr int QT3 = 64;            // queries per work unit
 
+// 16-byte asynchronous global -> shared copies (both addresses 16-byte aligned)
+__device__ __forceinline__ void cp_async16(void * dst, const void * src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                 :: "r"((uint32_t) __cvta_generic_to_shared(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
+
 template <int REP>
 constexpr int tiled_smem_floats() {
     return REP * D * QT3 + D * KT + KT * D + KT * QT3 * REP + QT3 * REP;
@@ -334,15 +343,29 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
         }
 
         // ---- pass 1
-        int lo4[4], fe4[4];
+        int lo4[4], hi4[4], fe4[4];
         float ml[4];
 #pragma unroll
         for (int a = 0; a < 4; ++a) {
             int lo, hi;
             range(qa + a, lo, hi);
             lo4[a] = lo;
+            hi4[a] = hi;
             fe4[a] = lo + ((hi - lo) & ~7);
             ml[a] = -INFINITY;
+        }
+        // keys that any of this warp's 32 queries sees: [w_lo, w_hi) (ranges grow with the row)
+        int w_lo = it.k0, w_hi = it.k0;
+        {
+            const int qb = 32 * (w4 & 1);
+            const int last = min(qb + 31, it.q1 - it.q0 - 1);
+            if (last >= qb) {
+                int l0, h0, l1, h1;
+                range(qb, l0, h0);
+                range(last, l1, h1);
+                w_lo = l0;
+                w_hi = h1;
+            }
         }
         const float (*Qh)[QT3] = Qs + hq * D;
         // key tiles: the next tile's rows are loaded into registers while this one is used
@@ -370,7 +393,14 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
             }
             __syncthreads();
             if (kt + KT < it.k1) kload(kt + KT);
+            // a warp whose 32 queries see none of its 16 keys (band layers) only stores zeros
+            const bool live = kt + kb - 4 * (lane >> 3) < w_hi && kt + kb - 4 * (lane >> 3) + 16 > w_lo;
             float y0123[4][4], x45[4][4], x6[4][4], x01[4][4], x2[4][4], x0[4][4], x4[4][4];
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int b2 = 0; b2 < 4; ++b2) x0[a][b2] = 0.0f;
+            if (live) {
 #pragma unroll
             for (int l = 0; l < 8; ++l) {
                 float acc[4][4];
@@ -408,16 +438,21 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
                         }
                     }
             }
+            }
+            // stored: the score inside the query's key range, 0 outside (pass 3 reads them as weights)
 #pragma unroll
             for (int b2 = 0; b2 < 4; ++b2) {
                 const int kj = kt + kb + b2;
                 if (kb + b2 < nk) {
-                    *(float4 *) (sc_base + (size_t) (kj - it.k0) * NQH + hq * QT3 + qa) =
-                        make_float4(x0[0][b2], x0[1][b2], x0[2][b2], x0[3][b2]);
+                    float sv[4];
 #pragma unroll
                     for (int a = 0; a < 4; ++a) {
+                        const bool in = kj >= lo4[a] && kj < hi4[a];
+                        sv[a] = in ? x0[a][b2] : 0.0f;
                         if (kj >= lo4[a] && kj < fe4[a]) ml[a] = (ml[a] < x0[a][b2]) ? x0[a][b2] : ml[a];
                     }
+                    *(float4 *) (sc_base + (size_t) (kj - it.k0) * NQH + hq * QT3 + qa) =
+                        make_float4(sv[0], sv[1], sv[2], sv[3]);
                 }
             }
         }
@@ -473,10 +508,12 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
 #pragma unroll
                 for (int z = 0; z < 16; ++z) x[z] = gp[(size_t) (8 * (gi + (z >> 2)) + (z & 3)) * NQH];
 #pragma unroll
-                for (int z = 0; z < 16; ++z) {
-                    const float e = exp8(__fsub_rn(x[z], m));
-                    vs[z & 3] = __fadd_rn(vs[z & 3], e);
-                    gp[(size_t) (8 * (gi + (z >> 2)) + (z & 3)) * NQH] = e;
+                for (int z = 0; z < 16; z += 2) {               // two exps per packed evaluation
+                    const float2 e = exp8x2(__fadd2_rn(make_float2(x[z], x[z + 1]), make_float2(-m, -m)));
+                    vs[z & 3] = __fadd_rn(vs[z & 3], e.x);
+                    vs[(z + 1) & 3] = __fadd_rn(vs[(z + 1) & 3], e.y);
+                    gp[(size_t) (8 * (gi + (z >> 2)) + (z & 3)) * NQH] = e.x;
+                    gp[(size_t) (8 * (gi + ((z + 1) >> 2)) + ((z + 1) & 3)) * NQH] = e.y;
                 }
             }
             for (; gi < ng; ++gi) {
@@ -506,54 +543,54 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
         }
         __syncthreads();
 
-        // ---- pass 3
-        int c_lo, c_hi;
-        range(c_qh % QT3, c_lo, c_hi);
-        const float c_inv = invs[c_qh];
+        // ---- pass 3: o = fma(e * inv, v, o) over the keys in order; e is 0 outside a query's range,
+        // and fma(0, v, o) leaves o unchanged.  Value rows and exps arrive by cp.async in a 2-stage
+        // ring laid over the shared memory of passes 1-2 (invs excepted).
         float2 o[4][4];                                            // [query][dim pair]
 #pragma unroll
         for (int a = 0; a < 4; ++a)
 #pragma unroll
             for (int z = 0; z < 4; ++z) o[a][z] = make_float2(0.0f, 0.0f);
-        // value rows and exps of the next tile are loaded into registers while this one is used
-        constexpr int VPT = KT * D / 4 / NT, EPT = KT * NQH / NT;
-        float4 vp[VPT];
-        float ep[EPT];
-        auto vload = [&](int kt) {
+        float inv4[4];
 #pragma unroll
-            for (int z = 0; z < VPT; ++z) {
-                const int i = tid + z * NT, j = i / (D / 4), d4 = i % (D / 4);
-                vp[z] = kt + j < it.k1 ? ((const float4 *) (vg + (ptrdiff_t) (kt + j) * D))[d4]
-                                       : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-#pragma unroll
-            for (int z = 0; z < EPT; ++z) {
-                const int kj = kt + tid / NQH + z * (NT / NQH);
-                ep[z] = (kj < it.k1 && kj >= c_lo && kj < c_hi) ? sc_base[(size_t) (kj - it.k0) * NQH + c_qh] : 0.0f;
-            }
-        };
-        vload(it.k0);
-        for (int kt = it.k0; kt < it.k1; kt += KT) {
+        for (int a = 0; a < 4; ++a) inv4[a] = invs[hq * QT3 + qa + a];
+        constexpr int STAGE = KT * D + KT * NQH;                   // V tile [KT][D], exps [KT][NQH]
+        static_assert(2 * STAGE <= REP * D * QT3 + 2 * D * KT + KT * NQH, "pass-3 ring overlaps invs");
+        auto issue = [&](int kt, int st) {
             const int nk = min(KT, it.k1 - kt);
-#pragma unroll
-            for (int z = 0; z < VPT; ++z) {
-                const int i = tid + z * NT, j = i / (D / 4), d4 = i % (D / 4);
-                ((float4 *) Vs[j])[d4] = vp[z];
+            float * sv = smem + st * STAGE;
+            float * se = sv + KT * D;
+            for (int i = tid; i < nk * (D / 4); i += NT) {
+                const int j = i / (D / 4), d4 = i % (D / 4);
+                cp_async16(sv + j * D + 4 * d4, vg + (ptrdiff_t) (kt + j) * D + 4 * d4);
             }
-            // weight = e * inv inside the query's range, 0 outside
-#pragma unroll
-            for (int z = 0; z < EPT; ++z) {
-                const int j = tid / NQH + z * (NT / NQH), kj = kt + j;
-                Cw[j][c_qh] = (kj < it.k1 && kj >= c_lo && kj < c_hi) ? __fmul_rn(ep[z], c_inv) : 0.0f;
+            const float * eg = sc_base + (size_t) (kt - it.k0) * NQH;
+            for (int i = tid; i < nk * (NQH / 4); i += NT) cp_async16(se + 4 * i, eg + 4 * i);
+            cp_async_commit();
+        };
+        issue(it.k0, 0);
+        int st = 0;
+        for (int kt = it.k0; kt < it.k1; kt += KT, st ^= 1) {
+            const int nk = min(KT, it.k1 - kt);
+            if (kt + KT < it.k1) {
+                issue(kt + KT, st ^ 1);
+                cp_async_wait<1>();
+            } else {
+                cp_async_wait<0>();
             }
             __syncthreads();
-            if (kt + KT < it.k1) vload(kt + KT);
+            const float * sv = smem + st * STAGE;
+            const float * se = sv + KT * D;
+            // only the keys some query of this warp sees (band layers skip the rest)
+            const int jlo = max(0, w_lo - kt), jhi = min(nk, w_hi - kt);
 #pragma unroll 2
-            for (int j = 0; j < nk; ++j) {
-                const float4 cv = *(const float4 *) &Cw[j][hq * QT3 + qa];
-                const float4 v0 = *(const float4 *) &Vs[j][db];
-                const float4 v1 = *(const float4 *) &Vs[j][db + 4];
-                const float cc[4] = {cv.x, cv.y, cv.z, cv.w};
+            for (int j = jlo; j < jhi; ++j) {
+                const float4 e = *(const float4 *) (se + j * NQH + hq * QT3 + qa);
+                const float2 c01 = __fmul2_rn(make_float2(e.x, e.y), make_float2(inv4[0], inv4[1]));
+                const float2 c23 = __fmul2_rn(make_float2(e.z, e.w), make_float2(inv4[2], inv4[3]));
+                const float cc[4] = {c01.x, c01.y, c23.x, c23.y};
+                const float4 v0 = *(const float4 *) (sv + j * D + db);
+                const float4 v1 = *(const float4 *) (sv + j * D + db + 4);
                 const float2 vv[4] = {make_float2(v0.x, v0.y), make_float2(v0.z, v0.w),
                                       make_float2(v1.x, v1.y), make_float2(v1.z, v1.w)};
 #pragma unroll

@@ -37,6 +37,29 @@ __device__ __forceinline__ float exp8(float x) {
     return __fmul_rn(y, __int_as_float(e));
 }
 
+// two lanes of exp256 at once: the same operations as exp8 on each component (the packed
+// multiply, add and fused multiply-add round each component as the scalar forms do)
+__device__ __forceinline__ float2 exp8x2(float2 x) {
+    x.x = fmaxf(fminf(x.x, 88.3762626647949f), -87.3f);
+    x.y = fmaxf(fminf(x.y, 88.3762626647949f), -87.3f);
+    const float2 t = __fmul2_rn(x, make_float2(1.44269504088896341f, 1.44269504088896341f));
+    const float2 fx = make_float2(rintf(t.x), rintf(t.y));
+    const float2 nfx = make_float2(-fx.x, -fx.y);
+    x = __ffma2_rn(nfx, make_float2(0.693359375f, 0.693359375f), x);
+    x = __ffma2_rn(nfx, make_float2(-2.12194440e-4f, -2.12194440e-4f), x);
+    const float2 z = __fmul2_rn(x, x);
+    float2 y = make_float2(1.9875691500e-4f, 1.9875691500e-4f);
+    y = __ffma2_rn(y, x, make_float2(1.3981999507e-3f, 1.3981999507e-3f));
+    y = __ffma2_rn(y, x, make_float2(8.3334519073e-3f, 8.3334519073e-3f));
+    y = __ffma2_rn(y, x, make_float2(4.1665795894e-2f, 4.1665795894e-2f));
+    y = __ffma2_rn(y, x, make_float2(1.6666665459e-1f, 1.6666665459e-1f));
+    y = __ffma2_rn(y, x, make_float2(5.0000001201e-1f, 5.0000001201e-1f));
+    y = __ffma2_rn(y, z, __fadd2_rn(x, make_float2(1.0f, 1.0f)));
+    const float2 p2 = make_float2(__int_as_float((__float2int_rn(fx.x) + 127) << 23),
+                                  __int_as_float((__float2int_rn(fx.y) + 127) << 23));
+    return __fmul2_rn(y, p2);
+}
+
 // one lane of tanh256 (:103-117)
 __device__ __forceinline__ float tanh8(float x) {
     const float ax = fabsf(x);
