@@ -62,6 +62,17 @@ NEXTERA_API int nxk_linear_i8(const int8_t * xq, const float * sx, int T, const 
 /* the same result from a plain CUDA-core kernel (validation only) */
 NEXTERA_API int nxk_linear_i8_simt(const int8_t * xq, const float * sx, int T, const int8_t * w8, const float * sw,
                                    int K, int N, const float * res, float * out, void * stream);
+/* The int8 linear followed by the row op the reference applies to its output and by quantize_row
+ * (:378-403) for the next int8 linear, in one kernel: codes q [T][N] (s8, the reference's u8 - 128)
+ * and scales sq [T][N/256]; N must be a multiple of 256.
+ *   relu_sqr_q:  v = relu(y)^2              (op_relu_sqr, :485-505)
+ *   gate_q:      v = sigmoid(y) * z[t][n]   (op_gate, :508-523), z [T][N] fp32
+ * Same codes and scales as nxk_linear_i8 then nxk_relu_sqr / nxk_gate with int8 output. */
+NEXTERA_API int nxk_linear_i8_relu_sqr_q(const int8_t * xq, const float * sx, int T, const int8_t * w8,
+                                         const float * sw, int K, int N, int8_t * q, float * sq, void * stream);
+NEXTERA_API int nxk_linear_i8_gate_q(const int8_t * xq, const float * sx, int T, const int8_t * w8,
+                                     const float * sw, int K, int N, const float * z, int8_t * q, float * sq,
+                                     void * stream);
 /* int32 block sums S_B, [T][N][n_blk] (validation of the integer path) */
 NEXTERA_API int nxk_block_sums(const int8_t * xq, int T, const int8_t * w8, int K, int N, int32_t * sums, void * stream);
 

@@ -33,6 +33,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <cstring>
 #include <mutex>
 
 namespace nxk {
@@ -52,10 +53,22 @@ constexpr int MAX_BLK = 12;                         // K <= 3072
 constexpr int SCALE_FLOATS = 2 * MAX_BLK * BN;           // one slot: sw [block][128 cols], sx [128 rows][block]
 constexpr int SCALE_BYTES = 2 * SCALE_FLOATS * 4;        // two slots
 constexpr int OUT_BYTES = EPI_WARPS * 32 * 64 * 4;       // each epilogue warp's 32 x 64 output slice (2 swizzled boxes)
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + SCALE_BYTES + 1024 /* alignment */ + 256 /* barriers */;
+constexpr int AMX_BYTES = 2 * 4 * 2 * 32 * 4;              // quantizing epilogues: [unit parity][quad][half][lane] maxima
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + SCALE_BYTES + AMX_BYTES + 1024 /* alignment */ +
+                           256 /* barriers */;
 constexpr uint32_t IDESC = idesc_i8(BM, BN);
 
 enum : int { ERR_PRODUCER = 0x101, ERR_MMA = 0x102, ERR_EPILOGUE = 0x103 };
+
+// Epilogues.  EPI_F32: fp32 output (TMA store, or TMA reduce-add into the residual).  The other two
+// finish the row op that the reference applies to the layer's output and quantize the result for the
+// next int8 layer (quantize_row, :378-403), writing codes and per-256-column scales instead of fp32:
+//   EPI_RELU2  v = relu(f)^2                (op_relu_sqr, :485-505)
+//   EPI_GATE   v = sigmoid(f) * z[t][n]      (op_gate, :508-523)
+// A quantization block is 256 columns, two 128-column tiles: a CTA takes the two as one unit, keeps the
+// first tile's values in shared memory, and the two warps that hold a row's halves exchange their
+// maxima through shared memory (an mbarrier with a bounded wait) before quantizing.
+enum : int { EPI_F32 = 0, EPI_RELU2 = 1, EPI_GATE = 2 };
 
 struct Args {
     const float * sx;
@@ -64,21 +77,34 @@ struct Args {
     float * out;
     int T, N, K, n_blk, n_chunks, tiles_n, n_tiles;
     int accumulate;          // 1: out += result (the residual is `out` itself), by TMA reduce-add
+    int n_units;             // tiles (EPI_F32) or pairs of tiles (quantizing epilogues) to process
+    const float * z;         // EPI_GATE: the multiplier [T][N]
+    int8_t * qout;           // quantizing epilogues: codes [T][N] (s8, the reference's u8 - 128)
+    float * sqout;           // and scales [T][N / 256]
 };
 
+__device__ __forceinline__ uint32_t pack_codes(float a, float b, float c, float d, float inv) {
+    return (uint32_t) (uint8_t) act_code(a, inv) | ((uint32_t) (uint8_t) act_code(b, inv) << 8) |
+           ((uint32_t) (uint8_t) act_code(c, inv) << 16) | ((uint32_t) (uint8_t) act_code(d, inv) << 24);
+}
+
+template <int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
            const __grid_constant__ CUtensorMap tm_out, const Args a) {
+    constexpr int SUB = EPI == EPI_F32 ? 1 : 2;                     // tiles per unit
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
     uint8_t * sA = smem;
     uint8_t * sB = smem + STAGES * A_BYTES;
     float * so = (float *) (sB + STAGES * B_BYTES);                   // [EPI_WARPS][2][32 rows][32 floats], 1024-aligned
     float * scl = (float *) ((uint8_t *) so + OUT_BYTES);             // [2][SCALE_FLOATS]
-    uint64_t * bars = (uint64_t *) ((uint8_t *) scl + SCALE_BYTES);
+    float * amx = (float *) ((uint8_t *) scl + SCALE_BYTES);          // [2][4][2][32]
+    uint64_t * bars = (uint64_t *) ((uint8_t *) amx + AMX_BYTES);
     uint64_t * full = bars, * empty = bars + STAGES, * accf = bars + 2 * STAGES, * acce = bars + 2 * STAGES + ACC;
     uint64_t * sfull = bars + 2 * STAGES + 2 * ACC, * sempty = sfull + 2;
-    uint32_t * tmem_slot = (uint32_t *) (sempty + 2);
+    uint64_t * xbar = sempty + 2;                                     // [4]: row-maximum exchange per quadrant
+    uint32_t * tmem_slot = (uint32_t *) (xbar + 4);
     volatile int * abort_flag = (volatile int *) (tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -95,11 +121,12 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
             mbar_init(smem_u32(&sfull[b]), 1);
             mbar_init(smem_u32(&sempty[b]), EPI_WARPS);
         }
+        for (int b = 0; b < 4; ++b) mbar_init(smem_u32(&xbar[b]), 2);
         *abort_flag = 0;
         fence_barrier_init();
         tma_prefetch_desc(&tm_a);
         tma_prefetch_desc(&tm_b);
-        tma_prefetch_desc(&tm_out);
+        if (EPI == EPI_F32) tma_prefetch_desc(&tm_out);
     }
     if (warp == 1) {
         tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
@@ -115,7 +142,9 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
         if (lane == 0) {
             uint32_t it = 0, tc = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x, ++tc) {
+            for (int t_ = SUB * blockIdx.x, u_ = 0; ok && t_ < a.n_tiles;
+                 t_ += (++u_ % SUB) ? 1 : SUB * (gridDim.x - 1) + 1, ++tc) {
+                const int tile = t_;
                 const int m0 = (tile / a.tiles_n) * BM, n0 = (tile % a.tiles_n) * BN;
                 {
                     // the tile's scales -> slot tc % 2: sw rows [block][n0, n0 + cols), sx rows [m0, m0 + rows)
@@ -161,7 +190,8 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
         if (lane == 0) {
             uint32_t it = 0, kb = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
+            for (int t_ = SUB * blockIdx.x, u_ = 0; ok && t_ < a.n_tiles;
+                 t_ += (++u_ % SUB) ? 1 : SUB * (gridDim.x - 1) + 1) {
                 for (int b = 0; ok && b < a.n_blk; ++b, ++kb) {
                     const uint32_t acc = kb % ACC, use = kb / ACC;
                     if (use > 0 && !mbar_wait(smem_u32(&acce[acc]), (use - 1) & 1)) { ok = false; break; }
@@ -196,9 +226,13 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
         // ------------------------------------------------------------ epilogue
         const int quad = warp & 3, halfc = (warp - 2) >> 2;
         const int row = 32 * quad + lane;
-        uint32_t kb = 0, tc = 0;
+        uint32_t kb = 0, tc = 0, uc = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x, ++tc) {
+        float am0 = 0.0f;                                              // quantizing: first tile's row maximum
+        for (int t_ = SUB * blockIdx.x, u_ = 0; ok && t_ < a.n_tiles;
+             t_ += (++u_ % SUB) ? 1 : SUB * (gridDim.x - 1) + 1, ++tc) {
+            const int tile = t_;
+            const int s2 = tile % SUB;                                 // which tile of the unit
             const int m0 = (tile / a.tiles_n) * BM, n0 = (tile % a.tiles_n) * BN;
             const int t = m0 + row;
             const int nc = n0 + 64 * halfc;
@@ -256,6 +290,74 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
             if (!ok) break;
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&sempty[sb]));             // scales slot free
+            if (EPI != EPI_F32) {
+                // the row op on this tile's 64 columns of row t, then its maximum |v|
+                if (EPI == EPI_RELU2) {
+#pragma unroll
+                    for (int c = 0; c < 32; ++c) {
+                        const float x0 = f[c].x > 0.0f ? f[c].x : 0.0f, x1 = f[c].y > 0.0f ? f[c].y : 0.0f;
+                        f[c] = __fmul2_rn(make_float2(x0, x1), make_float2(x0, x1));
+                    }
+                } else if (t < a.T) {
+                    const float4 * zr = (const float4 *) (a.z + (size_t) t * a.N + nc);
+#pragma unroll
+                    for (int c4 = 0; c4 < 16; ++c4) {
+                        const float4 zz = zr[c4];
+                        f[2 * c4] = make_float2(__fmul_rn(sigmoid8(f[2 * c4].x), zz.x),
+                                                __fmul_rn(sigmoid8(f[2 * c4].y), zz.y));
+                        f[2 * c4 + 1] = make_float2(__fmul_rn(sigmoid8(f[2 * c4 + 1].x), zz.z),
+                                                    __fmul_rn(sigmoid8(f[2 * c4 + 1].y), zz.w));
+                    }
+                }
+                float am = 0.0f;
+#pragma unroll
+                for (int c = 0; c < 32; ++c) am = fmaxf(am, fmaxf(fabsf(f[c].x), fabsf(f[c].y)));
+                float * rowp = so + (warp - 2) * 2048 + lane * 64;     // this warp's row, 16 swizzled chunks
+                if (s2 == 0) {
+                    // first tile of the unit: park the values until the second tile's are known
+#pragma unroll
+                    for (int c = 0; c < 16; ++c)
+                        *(float4 *) (rowp + 4 * (c ^ (lane & 7))) =
+                            make_float4(f[2 * c].x, f[2 * c].y, f[2 * c + 1].x, f[2 * c + 1].y);
+                    am0 = am;
+                    continue;
+                }
+                // second tile: the row's block maximum over both tiles and both column halves
+                const uint32_t p = uc & 1;
+                float * ax = amx + ((p * 4 + quad) * 2) * 32;            // [half][lane]
+                ax[halfc * 32 + lane] = fmaxf(am0, am);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&xbar[quad]));
+                {
+                    const bool got = mbar_wait(smem_u32(&xbar[quad]), p) && !*abort_flag;
+                    if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+                }
+                const float amax = fmaxf(ax[lane], ax[32 + lane]);
+                ++uc;
+                if (t < a.T) {
+                    const float inv = act_inv(amax);
+                    const int n00 = n0 - BN;                                // the unit's first column
+                    uint4 * q0 = (uint4 *) (a.qout + (size_t) t * a.N + n00 + 64 * halfc);
+                    uint4 * q1 = (uint4 *) (a.qout + (size_t) t * a.N + n0 + 64 * halfc);
+#pragma unroll
+                    for (int c4 = 0; c4 < 4; ++c4) {
+                        const float4 v0 = *(const float4 *) (rowp + 4 * ((4 * c4 + 0) ^ (lane & 7)));
+                        const float4 v1 = *(const float4 *) (rowp + 4 * ((4 * c4 + 1) ^ (lane & 7)));
+                        const float4 v2 = *(const float4 *) (rowp + 4 * ((4 * c4 + 2) ^ (lane & 7)));
+                        const float4 v3 = *(const float4 *) (rowp + 4 * ((4 * c4 + 3) ^ (lane & 7)));
+                        q0[c4] = make_uint4(pack_codes(v0.x, v0.y, v0.z, v0.w, inv), pack_codes(v1.x, v1.y, v1.z, v1.w, inv),
+                                            pack_codes(v2.x, v2.y, v2.z, v2.w, inv), pack_codes(v3.x, v3.y, v3.z, v3.w, inv));
+                        const float2 * g = &f[8 * c4];
+                        q1[c4] = make_uint4(pack_codes(g[0].x, g[0].y, g[1].x, g[1].y, inv),
+                                            pack_codes(g[2].x, g[2].y, g[3].x, g[3].y, inv),
+                                            pack_codes(g[4].x, g[4].y, g[5].x, g[5].y, inv),
+                                            pack_codes(g[6].x, g[6].y, g[7].x, g[7].y, inv));
+                    }
+                    if (halfc == 0) a.sqout[(size_t) t * (a.N / 256) + n00 / 256] = act_scale(amax);
+                }
+                __syncwarp();
+                continue;
+            }
             if (nc < a.N) {
                 // this warp's 32 x 64 slice -> shared memory (two 32 x 32 boxes in the 128-byte
                 // swizzle: 16-byte chunk c of row r at chunk c ^ (r % 8)) -> one TMA store or
@@ -367,6 +469,17 @@ int sm_count() {
     return n > 0 ? n : 148;
 }
 
+template <int EPI>
+int launch(const CUtensorMap & ma, const CUtensorMap & mb, const CUtensorMap & mo, const Args & a, cudaStream_t s) {
+    static std::once_flag attr_once;
+    std::call_once(attr_once, []() {
+        cudaFuncSetAttribute(gemm_i8_tc<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    });
+    const int grid = min(a.n_units, sm_count());
+    gemm_i8_tc<EPI><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, mo, a);
+    return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
+}
+
 } // namespace gemm
 } // namespace nxk
 
@@ -396,10 +509,6 @@ int nxk_linear_i8(const int8_t * xq, const float * sx, int T, const int8_t * w8,
             cudaSuccess) {
         return NXK_ELAUNCH;
     }
-    static std::once_flag attr_once;
-    std::call_once(attr_once, []() {
-        cudaFuncSetAttribute(gemm_i8_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    });
     Args a;
     a.sx = sx; a.sw = sw; a.res = res; a.out = out;
     a.accumulate = res ? 1 : 0;
@@ -408,9 +517,47 @@ int nxk_linear_i8(const int8_t * xq, const float * sx, int T, const int8_t * w8,
     a.n_chunks = (K + BKB - 1) / BKB;
     a.tiles_n = (N + BN - 1) / BN;
     a.n_tiles = ((T + BM - 1) / BM) * a.tiles_n;
-    const int grid = min(a.n_tiles, sm_count());
-    gemm_i8_tc<<<grid, THREADS, SMEM_BYTES, (cudaStream_t) stream>>>(ma, mb, mo, a);
-    return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
+    a.n_units = a.n_tiles;
+    a.z = nullptr; a.qout = nullptr; a.sqout = nullptr;
+    return launch<EPI_F32>(ma, mb, mo, a, (cudaStream_t) stream);
+}
+
+// int8 linear whose output goes through relu^2 (op = EPI_RELU2) or sigmoid(.) * z (EPI_GATE) and is
+// quantized for the next int8 linear: codes [T][N] and scales [T][N / 256]; N % 256 == 0.
+static int linear_q(int op, const int8_t * xq, const float * sx, int T, const int8_t * w8, const float * sw, int K,
+                    int N, const float * z, int8_t * q, float * sq, cudaStream_t stream) {
+    using namespace nxk::gemm;
+    if (T < 0 || K <= 0 || N <= 0 || (K & 31) || (N % 256) || !xq || !w8 || !sx || !sw || !q || !sq) return NXK_EINVAL;
+    if (op == EPI_GATE && (!z || ((uintptr_t) z & 15))) return NXK_EINVAL;
+    if ((K + I8_BLOCK - 1) / I8_BLOCK > MAX_BLK) return NXK_EINVAL;
+    if (((uintptr_t) xq & 15) || ((uintptr_t) w8 & 15) || ((uintptr_t) sw & 15) || ((uintptr_t) q & 15))
+        return NXK_EINVAL;
+    if (T == 0) return NXK_OK;
+    CUtensorMap ma, mb, mo;
+    memset(&mo, 0, sizeof(mo));                       // no fp32 output: the map is never used
+    if (!make_map(&ma, xq, (uint64_t) T, (uint64_t) K) || !make_map(&mb, w8, (uint64_t) N, (uint64_t) K))
+        return NXK_ELAUNCH;
+    Args a;
+    a.sx = sx; a.sw = sw; a.res = nullptr; a.out = nullptr;
+    a.accumulate = 0;
+    a.T = T; a.N = N; a.K = K;
+    a.n_blk = (K + I8_BLOCK - 1) / I8_BLOCK;
+    a.n_chunks = (K + BKB - 1) / BKB;
+    a.tiles_n = N / BN;
+    a.n_tiles = ((T + BM - 1) / BM) * a.tiles_n;
+    a.n_units = a.n_tiles / 2;
+    a.z = z; a.qout = q; a.sqout = sq;
+    return op == EPI_RELU2 ? launch<EPI_RELU2>(ma, mb, mo, a, stream) : launch<EPI_GATE>(ma, mb, mo, a, stream);
+}
+
+int nxk_linear_i8_relu_sqr_q(const int8_t * xq, const float * sx, int T, const int8_t * w8, const float * sw, int K,
+                             int N, int8_t * q, float * sq, void * stream) {
+    return linear_q(nxk::gemm::EPI_RELU2, xq, sx, T, w8, sw, K, N, nullptr, q, sq, (cudaStream_t) stream);
+}
+
+int nxk_linear_i8_gate_q(const int8_t * xq, const float * sx, int T, const int8_t * w8, const float * sw, int K, int N,
+                         const float * z, int8_t * q, float * sq, void * stream) {
+    return linear_q(nxk::gemm::EPI_GATE, xq, sx, T, w8, sw, K, N, z, q, sq, (cudaStream_t) stream);
 }
 
 int nxk_linear_i8_simt(const int8_t * xq, const float * sx, int T, const int8_t * w8, const float * sw, int K, int N,

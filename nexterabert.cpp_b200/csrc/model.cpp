@@ -630,6 +630,24 @@ public:
                    name.c_str());
     }
 
+    // y = W x followed by relu^2 (z == nullptr) or sigmoid(y) * z, quantized for the next linear:
+    // codes and scales out; false when the shape needs the separate row op (N % 256 != 0)
+    bool linear_q(const std::string & name, const int8_t * q, const float * sx, int T, const float * z,
+                  int8_t * qo, float * so) {
+        if (!ok) return true;
+        auto it = c_.i8.find(name);
+        if (it == c_.i8.end() || it->second.n_out % 256 != 0) return false;
+        mark(PROF_LINEAR);
+        ++c_.launches;
+        const I8Weight & w = it->second;
+        const int rc = z ? nxk_linear_i8_gate_q(q, sx, T, w.w.as<int8_t>(), w.scale.as<float>(), w.n_in, w.n_out, z, qo,
+                                                so, s_)
+                         : nxk_linear_i8_relu_sqr_q(q, sx, T, w.w.as<int8_t>(), w.scale.as<float>(), w.n_in,
+                                                    w.n_out, qo, so, s_);
+        ok = check(rc, name.c_str());
+        return true;
+    }
+
     int n_out(const std::string & name) const {
         auto it = c_.i8.find(name);
         return it == c_.i8.end() ? 0 : it->second.n_out;
@@ -958,6 +976,11 @@ int run_encoder(nextera_context & c, const Batch & b, float rope0_base, const in
     auto gated_out = [&](const std::string & pre, const float * y, const float * z, float * gl) {
         fw.mark(PROF_ROWS);
         fw.rows(nxk_quantize(y, T, C, Q1, Q1s, s), "quantize");
+        // c_gate, the gate and its quantization in one kernel (codes to Q2, free by now)
+        if (fw.linear_q(pre + "c_gate.weight", Q1, Q1s, T, z, Q2, Q2s)) {
+            fw.linear(pre + "c_proj.weight", Q2, Q2s, T, X, X);   // x += c_proj(...), in place
+            return;
+        }
         fw.linear(pre + "c_gate.weight", Q1, Q1s, T, nullptr, gl);
         fw.mark(PROF_ROWS);
         fw.rows(nxk_gate(gl, z, T, C, nullptr, Q1, Q1s, s), "gate");
@@ -1026,9 +1049,12 @@ int run_encoder(nextera_context & c, const Batch & b, float rope0_base, const in
         fw.mark(PROF_ROWS);
         fw.rows(nxk_rms_norm(X, fw.p(blk + "mlp_norm.weight"), hp.rms_eps, T, C, nullptr, Q2, Q2s, s), "rms_norm");
         const int I = fw.n_out(blk + "mlp.c_fc.weight");
-        fw.linear(blk + "mlp.c_fc.weight", Q2, Q2s, T, nullptr, U);
-        fw.mark(PROF_ROWS);
-        fw.rows(nxk_relu_sqr(U, T, I, nullptr, Q1, Q1s, s), "relu_sqr");
+        // c_fc, relu^2 and its quantization in one kernel when I is a multiple of 256
+        if (!fw.linear_q(blk + "mlp.c_fc.weight", Q2, Q2s, T, nullptr, Q1, Q1s)) {
+            fw.linear(blk + "mlp.c_fc.weight", Q2, Q2s, T, nullptr, U);
+            fw.mark(PROF_ROWS);
+            fw.rows(nxk_relu_sqr(U, T, I, nullptr, Q1, Q1s, s), "relu_sqr");
+        }
         fw.linear(blk + "mlp.c_proj.weight", Q1, Q1s, T, X, X);      // x += c_proj(...), in place
     }
     if (!fw.ok) return 3;

@@ -48,6 +48,8 @@ def load_lib(path=None):
         "nxk_linear_i8": ([vp, vp, c_int, vp, vp, c_int, c_int, vp, vp, vp], c_int),
         "nxk_linear_i8_simt": ([vp, vp, c_int, vp, vp, c_int, c_int, vp, vp, vp], c_int),
         "nxk_block_sums": ([vp, c_int, vp, c_int, c_int, vp, vp], c_int),
+        "nxk_linear_i8_relu_sqr_q": ([vp, vp, c_int, vp, vp, c_int, c_int, vp, vp, vp], c_int),
+        "nxk_linear_i8_gate_q": ([vp, vp, c_int, vp, vp, c_int, c_int, vp, vp, vp, vp], c_int),
         "nxk_quantize": ([vp, c_int, c_int, vp, vp, vp], c_int),
         "nxk_rms_norm": ([vp, vp, c_float, c_int, c_int, vp, vp, vp, vp], c_int),
         "nxk_relu_sqr": ([vp, c_int, c_int, vp, vp, vp, vp], c_int),

@@ -97,6 +97,33 @@ def test_linear_shapes(ops, oracle, T, K, N):
     assert np.array_equal(ops.linear(xq, xs, w8, sw, res), want)
 
 
+@pytest.mark.parametrize("T,K,N", [(1, 256, 256), (300, 1024, 512), (129, 2304, 1024), (1000, 1024, 2304),
+                                   (4097, 1024, 256)])
+def test_linear_fused_row_op_quantize_bit_exact(ops, oracle, T, K, N):
+    """linear + relu^2 + quantize and linear + gate + quantize in one kernel: the codes and scales of the
+    separate ops (rows past the last full tile, a single row, 1 to 9 quantization blocks)"""
+    import torch
+    from gpulib import P, dev, host, stream_ptr
+    rng = np.random.default_rng(7 * T + K + N)
+    x = rng.standard_normal((T, K)).astype(np.float32)
+    w = (0.02 * rng.standard_normal((N, K))).astype(np.float32)
+    z = rng.standard_normal((T, N)).astype(np.float32)
+    w8, sw, _ = oracle.build_i8_weight(int(QT.Q8_0), sm.quantize_rows(w, QT.Q8_0), K, N)
+    xq, xs = oracle.quantize_rows(x)
+    y = oracle.linear_i8(xq, xs, w8, sw, None)
+    args = [P(dev(xq)), P(dev(xs)), T, P(dev(w8)), P(dev(sw)), K, N]
+    for name, want_v, extra in (("nxk_linear_i8_relu_sqr_q", oracle.relu_sqr(y), []),
+                                ("nxk_linear_i8_gate_q", oracle.gate(y, z), [P(dev(z))])):
+        q, sq = ops.quant_out(T, N)
+        q.fill_(0x55)
+        sq.fill_(float("nan"))
+        ops._ok(getattr(ops.L, name)(*args, *extra, P(q), P(sq), stream_ptr()), name)
+        wq, ws = oracle.quantize_rows(want_v)
+        gq, gs = host(q), host(sq)
+        assert np.array_equal(gq, wq), f"{name}: {np.count_nonzero(gq != wq)} codes differ"
+        assert np.array_equal(gs, ws), f"{name}: scales differ"
+
+
 @pytest.mark.parametrize("C", [512, 352])
 def test_quantize_and_row_ops_bit_exact(ops, oracle, C):
     """C = 352: a partial last 256-column block"""
