@@ -499,7 +499,7 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
                 m = (m < o) ? o : m;
             }
             // whole groups: this thread's lanes 4 * sub .. 4 * sub + 3, summed per lane in key order
-            float vs[4] = {0.f, 0.f, 0.f, 0.f};
+            float2 vs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};   // lanes (0,1), (2,3) of this thread
             const int ng = n >> 3;
             float * gp = sp + (size_t) (lo - it.k0 + 4 * p_sub) * NQH;
             int gi = 0;
@@ -508,24 +508,25 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
 #pragma unroll
                 for (int z = 0; z < 16; ++z) x[z] = gp[(size_t) (8 * (gi + (z >> 2)) + (z & 3)) * NQH];
 #pragma unroll
-                for (int z = 0; z < 16; z += 2) {               // two exps per packed evaluation
-                    const float2 e = exp8x2(__fadd2_rn(make_float2(x[z], x[z + 1]), make_float2(-m, -m)));
-                    vs[z & 3] = __fadd_rn(vs[z & 3], e.x);
-                    vs[(z + 1) & 3] = __fadd_rn(vs[(z + 1) & 3], e.y);
+                for (int z = 0; z < 16; z += 2) {               // two exps per packed evaluation; s - m <= 0
+                    const float2 e = exp8x2<true>(__fadd2_rn(make_float2(x[z], x[z + 1]), make_float2(-m, -m)));
+                    vs2[(z >> 1) & 1] = __fadd2_rn(vs2[(z >> 1) & 1], e);
                     gp[(size_t) (8 * (gi + (z >> 2)) + (z & 3)) * NQH] = e.x;
                     gp[(size_t) (8 * (gi + ((z + 1) >> 2)) + ((z + 1) & 3)) * NQH] = e.y;
                 }
             }
             for (; gi < ng; ++gi) {
 #pragma unroll
-                for (int z = 0; z < 4; ++z) {
-                    float * p = gp + (size_t) (8 * gi + z) * NQH;
-                    const float e = exp8(__fsub_rn(*p, m));
-                    vs[z] = __fadd_rn(vs[z], e);
-                    *p = e;
+                for (int z = 0; z < 4; z += 2) {
+                    float * p0 = gp + (size_t) (8 * gi + z) * NQH, * p1 = p0 + NQH;
+                    const float2 e = exp8x2<true>(__fadd2_rn(make_float2(*p0, *p1), make_float2(-m, -m)));
+                    vs2[z >> 1] = __fadd2_rn(vs2[z >> 1], e);
+                    *p0 = e.x;
+                    *p1 = e.y;
                 }
             }
             // sum = ((v0+v4)+(v2+v6)) + ((v1+v5)+(v3+v7)); lanes 4-7 are the partner's 0-3
+            const float vs[4] = {vs2[0].x, vs2[0].y, vs2[1].x, vs2[1].y};
             float w[4];
 #pragma unroll
             for (int z = 0; z < 4; ++z) w[z] = __shfl_xor_sync(0xffffffffu, vs[z], 1);

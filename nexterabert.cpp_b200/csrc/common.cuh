@@ -39,9 +39,15 @@ __device__ __forceinline__ float exp8(float x) {
 
 // two lanes of exp256 at once: the same operations as exp8 on each component (the packed
 // multiply, add and fused multiply-add round each component as the scalar forms do)
+// NONPOS: the arguments are known to be <= 0, where exp256's upper clamp is the identity.
+template <bool NONPOS = false>
 __device__ __forceinline__ float2 exp8x2(float2 x) {
-    x.x = fmaxf(fminf(x.x, 88.3762626647949f), -87.3f);
-    x.y = fmaxf(fminf(x.y, 88.3762626647949f), -87.3f);
+    if (!NONPOS) {
+        x.x = fminf(x.x, 88.3762626647949f);
+        x.y = fminf(x.y, 88.3762626647949f);
+    }
+    x.x = fmaxf(x.x, -87.3f);
+    x.y = fmaxf(x.y, -87.3f);
     const float2 t = __fmul2_rn(x, make_float2(1.44269504088896341f, 1.44269504088896341f));
     const float2 fx = make_float2(rintf(t.x), rintf(t.y));
     const float2 nfx = make_float2(-fx.x, -fx.y);
