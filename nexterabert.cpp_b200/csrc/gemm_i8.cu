@@ -83,9 +83,28 @@ struct Args {
     float * sqout;           // and scales [T][N / 256]
 };
 
-__device__ __forceinline__ uint32_t pack_codes(float a, float b, float c, float d, float inv) {
+// act_code of four values packed in a word.  `fast`: inv = 127 / amax is finite and |value| <= amax,
+// so |value * inv| <= 127.00002 and rounding to nearest is already the code (the reference's
+// saturation cannot trigger); a NaN product still gives the reference's -128.
+__device__ __forceinline__ uint32_t code_fast(float v) {
+    const int c = __float2int_rn(v);
+    return (uint32_t) (v == v ? c : -128) & 0xffu;
+}
+__device__ __forceinline__ uint32_t pack_codes(float a, float b, float c, float d, float inv, bool fast) {
+    if (fast) {
+        const float2 p = __fmul2_rn(make_float2(a, b), make_float2(inv, inv));
+        const float2 q = __fmul2_rn(make_float2(c, d), make_float2(inv, inv));
+        return code_fast(p.x) | (code_fast(p.y) << 8) | (code_fast(q.x) << 16) | (code_fast(q.y) << 24);
+    }
     return (uint32_t) (uint8_t) act_code(a, inv) | ((uint32_t) (uint8_t) act_code(b, inv) << 8) |
            ((uint32_t) (uint8_t) act_code(c, inv) << 16) | ((uint32_t) (uint8_t) act_code(d, inv) << 24);
+}
+
+// sigmoid256 (src/nexterabert.cpp:119-122) of two values: 1 / (1 + exp256(0 - x))
+__device__ __forceinline__ float2 sigmoid8x2(float2 x) {
+    const float2 e = exp8x2(__fadd2_rn(make_float2(0.0f, 0.0f), make_float2(-x.x, -x.y)));
+    const float2 d = __fadd2_rn(make_float2(1.0f, 1.0f), e);
+    return make_float2(__fdiv_rn(1.0f, d.x), __fdiv_rn(1.0f, d.y));
 }
 
 template <int EPI>
@@ -303,10 +322,8 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
 #pragma unroll
                     for (int c4 = 0; c4 < 16; ++c4) {
                         const float4 zz = zr[c4];
-                        f[2 * c4] = make_float2(__fmul_rn(sigmoid8(f[2 * c4].x), zz.x),
-                                                __fmul_rn(sigmoid8(f[2 * c4].y), zz.y));
-                        f[2 * c4 + 1] = make_float2(__fmul_rn(sigmoid8(f[2 * c4 + 1].x), zz.z),
-                                                    __fmul_rn(sigmoid8(f[2 * c4 + 1].y), zz.w));
+                        f[2 * c4] = __fmul2_rn(sigmoid8x2(f[2 * c4]), make_float2(zz.x, zz.y));
+                        f[2 * c4 + 1] = __fmul2_rn(sigmoid8x2(f[2 * c4 + 1]), make_float2(zz.z, zz.w));
                     }
                 }
                 float am = 0.0f;
@@ -336,6 +353,7 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
                 ++uc;
                 if (t < a.T) {
                     const float inv = act_inv(amax);
+                    const bool fast = isfinite(inv);
                     const int n00 = n0 - BN;                                // the unit's first column
                     uint4 * q0 = (uint4 *) (a.qout + (size_t) t * a.N + n00 + 64 * halfc);
                     uint4 * q1 = (uint4 *) (a.qout + (size_t) t * a.N + n0 + 64 * halfc);
@@ -345,13 +363,13 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
                         const float4 v1 = *(const float4 *) (rowp + 4 * ((4 * c4 + 1) ^ (lane & 7)));
                         const float4 v2 = *(const float4 *) (rowp + 4 * ((4 * c4 + 2) ^ (lane & 7)));
                         const float4 v3 = *(const float4 *) (rowp + 4 * ((4 * c4 + 3) ^ (lane & 7)));
-                        q0[c4] = make_uint4(pack_codes(v0.x, v0.y, v0.z, v0.w, inv), pack_codes(v1.x, v1.y, v1.z, v1.w, inv),
-                                            pack_codes(v2.x, v2.y, v2.z, v2.w, inv), pack_codes(v3.x, v3.y, v3.z, v3.w, inv));
+                        q0[c4] = make_uint4(pack_codes(v0.x, v0.y, v0.z, v0.w, inv, fast), pack_codes(v1.x, v1.y, v1.z, v1.w, inv, fast),
+                                            pack_codes(v2.x, v2.y, v2.z, v2.w, inv, fast), pack_codes(v3.x, v3.y, v3.z, v3.w, inv, fast));
                         const float2 * g = &f[8 * c4];
-                        q1[c4] = make_uint4(pack_codes(g[0].x, g[0].y, g[1].x, g[1].y, inv),
-                                            pack_codes(g[2].x, g[2].y, g[3].x, g[3].y, inv),
-                                            pack_codes(g[4].x, g[4].y, g[5].x, g[5].y, inv),
-                                            pack_codes(g[6].x, g[6].y, g[7].x, g[7].y, inv));
+                        q1[c4] = make_uint4(pack_codes(g[0].x, g[0].y, g[1].x, g[1].y, inv, fast),
+                                            pack_codes(g[2].x, g[2].y, g[3].x, g[3].y, inv, fast),
+                                            pack_codes(g[4].x, g[4].y, g[5].x, g[5].y, inv, fast),
+                                            pack_codes(g[6].x, g[6].y, g[7].x, g[7].y, inv, fast));
                     }
                     if (halfc == 0) a.sqout[(size_t) t * (a.N / 256) + n00 / 256] = act_scale(amax);
                 }

@@ -976,11 +976,8 @@ int run_encoder(nextera_context & c, const Batch & b, float rope0_base, const in
     auto gated_out = [&](const std::string & pre, const float * y, const float * z, float * gl) {
         fw.mark(PROF_ROWS);
         fw.rows(nxk_quantize(y, T, C, Q1, Q1s, s), "quantize");
-        // c_gate, the gate and its quantization in one kernel (codes to Q2, free by now)
-        if (fw.linear_q(pre + "c_gate.weight", Q1, Q1s, T, z, Q2, Q2s)) {
-            fw.linear(pre + "c_proj.weight", Q2, Q2s, T, X, X);   // x += c_proj(...), in place
-            return;
-        }
+        // (nxk_linear_i8_gate_q fuses the next two steps but is slower here: each epilogue lane
+        // reads its own row of z, 32 rows per warp load)
         fw.linear(pre + "c_gate.weight", Q1, Q1s, T, nullptr, gl);
         fw.mark(PROF_ROWS);
         fw.rows(nxk_gate(gl, z, T, C, nullptr, Q1, Q1s, s), "gate");

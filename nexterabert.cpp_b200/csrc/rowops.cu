@@ -237,17 +237,31 @@ __global__ void __launch_bounds__(256) conv_kernel(const float * __restrict__ x,
     const int t0 = blockIdx.x * CONV_ROWS, cb = blockIdx.y * 256;
     const int ncol = min(256, C - cb);
     const int hk = k / 2;
-    for (int i = threadIdx.x; i < n_rows * 64; i += blockDim.x) {
-        const int rr = i >> 6, c4 = i & 63;
-        const int tr = t0 - hk + rr;
-        if (tr < -halo || tr >= T + halo || 4 * c4 >= ncol) continue;   // rows that exist
-        const ptrdiff_t off = (ptrdiff_t) tr * C + cb + 4 * c4;
-        float4 xv = *(const float4 *) (x + off);
-        if (LILY) {
-            const float4 av = *(const float4 *) (a + off);
-            xv = make_float4(__fmul_rn(av.x, xv.x), __fmul_rn(av.y, xv.y), __fmul_rn(av.z, xv.z), __fmul_rn(av.w, xv.w));
+    // staged in batches of 3 items per thread, every load of a batch issued before its first use
+    for (int i0 = threadIdx.x; i0 < n_rows * 64; i0 += 3 * blockDim.x) {
+        float4 xv[3], av[3];
+        bool ok[3];
+#pragma unroll
+        for (int z = 0; z < 3; ++z) {
+            const int i = i0 + z * blockDim.x;
+            const int rr = i >> 6, c4 = i & 63;
+            const int tr = t0 - hk + rr;
+            ok[z] = i < n_rows * 64 && tr >= -halo && tr < T + halo && 4 * c4 < ncol;   // rows that exist
+            if (ok[z]) {
+                const ptrdiff_t off = (ptrdiff_t) tr * C + cb + 4 * c4;
+                xv[z] = *(const float4 *) (x + off);
+                if (LILY) av[z] = *(const float4 *) (a + off);
+            }
         }
-        ((float4 *) P)[i] = xv;
+#pragma unroll
+        for (int z = 0; z < 3; ++z) {
+            if (!ok[z]) continue;
+            float4 p = xv[z];
+            if (LILY)
+                p = make_float4(__fmul_rn(av[z].x, p.x), __fmul_rn(av[z].y, p.y), __fmul_rn(av[z].z, p.z),
+                                __fmul_rn(av[z].w, p.w));
+            ((float4 *) P)[i0 + z * blockDim.x] = p;
+        }
     }
     for (int i = threadIdx.x; i < k * 64; i += blockDim.x) {
         const int j = i >> 6, c4 = i & 63;
@@ -503,29 +517,36 @@ __global__ void pool_finish_kernel(int n, int C, int normalize, float * __restri
 // ---------------------------------------------------------------------------
 constexpr int ERR_TOKEN_RANGE = 0x201;
 
-__global__ void embed_kernel(int type, const uint8_t * __restrict__ table, size_t row_bytes, int n_rows, int C,
-                             const int32_t * __restrict__ tokens, int T, int ttype, const uint8_t * __restrict__ ttable,
-                             size_t trow_bytes, int tn_rows, const int32_t * __restrict__ types,
-                             float * __restrict__ out) {
-    const size_t i = blockIdx.x * (size_t) blockDim.x + threadIdx.x;
-    if (i >= (size_t) T * C) return;
-    const int t = (int) (i / C), c = (int) (i % C);
+// one block per token row; threads stride over its C columns
+__global__ void __launch_bounds__(256) embed_kernel(int type, const uint8_t * __restrict__ table, size_t row_bytes,
+                                                    int n_rows, int C, const int32_t * __restrict__ tokens, int T,
+                                                    int ttype, const uint8_t * __restrict__ ttable, size_t trow_bytes,
+                                                    int tn_rows, const int32_t * __restrict__ types,
+                                                    float * __restrict__ out) {
+    const int t = blockIdx.x;
+    if (t >= T) return;
     const int id = tokens[t];
+    float * o = out + (size_t) t * C;
     if (id < 0 || id >= n_rows) {
-        out[i] = 0.0f;
-        if (c == 0) atomicExch(&g_error, ERR_TOKEN_RANGE);
+        for (int c = threadIdx.x; c < C; c += blockDim.x) o[c] = 0.0f;
+        if (threadIdx.x == 0) atomicExch(&g_error, ERR_TOKEN_RANGE);
         return;
     }
-    float v = deq_elem(type, table + row_bytes * (size_t) id, c);
+    const uint8_t * row = table + row_bytes * (size_t) id;
+    int ty = -1;
     if (ttable) {
-        const int ty = types[t];
+        ty = types[t];
         if (ty < 0 || ty >= tn_rows) {
-            if (c == 0) atomicExch(&g_error, ERR_TOKEN_RANGE);
-        } else {
-            v = __fadd_rn(v, deq_elem(ttype, ttable + trow_bytes * (size_t) ty, c));
+            if (threadIdx.x == 0) atomicExch(&g_error, ERR_TOKEN_RANGE);
+            ty = -1;
         }
     }
-    out[i] = v;
+    const uint8_t * trow = ty >= 0 ? ttable + trow_bytes * (size_t) ty : nullptr;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        float v = deq_elem(type, row, c);
+        if (trow) v = __fadd_rn(v, deq_elem(ttype, trow, c));
+        o[c] = v;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -720,8 +741,7 @@ int nxk_embed(int type, const void * table, int n_rows, int C, const int32_t * t
     if (T == 0) return NXK_OK;
     const size_t rb = (size_t) (C / bs) * type_size(type);
     const size_t trb = ttable ? (size_t) (C / blck_size(ttype)) * type_size(ttype) : 0;
-    const size_t n = (size_t) T * C;
-    embed_kernel<<<(unsigned) ((n + 255) / 256), 256, 0, S(stream)>>>(
+    embed_kernel<<<(unsigned) T, 256, 0, S(stream)>>>(
         type, (const uint8_t *) table, rb, n_rows, C, tokens, T, ttype, (const uint8_t *) ttable, trb, tn_rows, types,
         out);
     return launched();
