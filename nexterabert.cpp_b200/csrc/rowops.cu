@@ -221,7 +221,9 @@ constexpr int CONV_KMAX = 64;
 
 inline size_t conv_smem_bytes(int k) { return sizeof(float) * 256 * (size_t) (CONV_ROWS + 2 * k - 1); }
 
-template <bool LILY>
+// KS > 0: the tap count is KS, and each lane keeps its 8 columns' taps in registers for rows whose
+// taps all lie inside their document (the rest read them from shared memory)
+template <bool LILY, int KS>
 __global__ void __launch_bounds__(256) conv_kernel(const float * __restrict__ x, const float * __restrict__ a,
                                                    const float * __restrict__ r, const float * __restrict__ b,
                                                    const float * __restrict__ taps, int k, int halo,
@@ -272,6 +274,11 @@ __global__ void __launch_bounds__(256) conv_kernel(const float * __restrict__ x,
     const int c0 = 8 * lane;
     const bool on = c0 < ncol;
     const int n_blk = (C + I8_BLOCK - 1) / I8_BLOCK;
+    float wr[KS > 0 ? KS : 1][8];
+    if (KS > 0 && on) {
+#pragma unroll
+        for (int j = 0; j < (KS > 0 ? KS : 1); ++j) ld8(W + (size_t) j * 256 + c0, wr[j]);
+    }
     for (int rr = warp; rr < CONV_ROWS; rr += (int) (blockDim.x >> 5)) {
         const int t = t0 + rr;
         if (t >= T) break;
@@ -280,17 +287,27 @@ __global__ void __launch_bounds__(256) conv_kernel(const float * __restrict__ x,
         const int j0 = max(0, lo - (t - hk)), j1 = min(k, hi - (t - hk));
         float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         if (on) {
+            float bv[8];
+            if (LILY) ld8(b + (size_t) t * C + cb + c0, bv);          // issued before the tap loop
             if (!LILY && r) ld8(r + (size_t) t * C + cb + c0, v);
-            for (int j = j0; j < j1; ++j) {
-                float pv[8], wv[8];
-                ld8(P + (size_t) (rr + j) * 256 + c0, pv);
-                ld8(W + (size_t) j * 256 + c0, wv);
+            if (KS > 0 && j0 == 0 && j1 == KS) {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) v[e] = __fmaf_rn(wv[e], pv[e], v[e]);
+                for (int j = 0; j < (KS > 0 ? KS : 1); ++j) {
+                    float pv[8];
+                    ld8(P + (size_t) (rr + j) * 256 + c0, pv);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) v[e] = __fmaf_rn(wr[j][e], pv[e], v[e]);
+                }
+            } else {
+                for (int j = j0; j < j1; ++j) {
+                    float pv[8], wv[8];
+                    ld8(P + (size_t) (rr + j) * 256 + c0, pv);
+                    ld8(W + (size_t) j * 256 + c0, wv);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) v[e] = __fmaf_rn(wv[e], pv[e], v[e]);
+                }
             }
             if (LILY) {
-                float bv[8];
-                ld8(b + (size_t) t * C + cb + c0, bv);
 #pragma unroll
                 for (int e = 0; e < 8; ++e) v[e] = __fmul_rn(v[e], bv[e]);
             }
@@ -307,14 +324,16 @@ int launch_conv(bool lily, const float * x, const float * a, const float * r, co
     if (T == 0) return NXK_OK;
     const dim3 grid((unsigned) ((T + CONV_ROWS - 1) / CONV_ROWS), (unsigned) ((C + 255) / 256));
     const size_t smem = conv_smem_bytes(k);
+    auto go = [&](auto kern, const float * a_, const float * r_, const float * b_) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+        kern<<<grid, 256, smem, s>>>(x, a_, r_, b_, taps, k, halo, row_doc, doc_start, doc_len, T, C, out, q, sx);
+    };
     if (lily) {
-        cudaFuncSetAttribute(conv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
-        conv_kernel<true><<<grid, 256, smem, s>>>(x, a, nullptr, b, taps, k, halo, row_doc, doc_start, doc_len, T, C,
-                                                 out, q, sx);
+        if (k == 5) go(conv_kernel<true, 5>, a, nullptr, b);
+        else go(conv_kernel<true, 0>, a, nullptr, b);
     } else {
-        cudaFuncSetAttribute(conv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
-        conv_kernel<false><<<grid, 256, smem, s>>>(x, nullptr, r, nullptr, taps, k, halo, row_doc, doc_start, doc_len,
-                                                  T, C, out, q, sx);
+        if (k == 5) go(conv_kernel<false, 5>, nullptr, r, nullptr);
+        else go(conv_kernel<false, 0>, nullptr, r, nullptr);
     }
     return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
 }
