@@ -137,6 +137,22 @@ NEXTERA_API int nxk_pool(const float * hidden, const int32_t * doc_start, const 
 NEXTERA_API int nxk_pool_continue(const float * hidden, int T, int C, float * pooled, void * stream);
 NEXTERA_API int nxk_pool_finish(int n, int C, int normalize, float * pooled, void * stream);
 
+/* ---- heads (builder::transform / pooler / classifier :1296-1317, nextera_mlm_logits :1963-2011) ---- */
+/* transform's tail: GELU(erf) (ggml_gelu_erf), then ggml_norm * w (w may be NULL); out may be x */
+NEXTERA_API int nxk_gelu_norm(const float * x, const float * w, float eps, int T, int C, float * out, void * stream);
+/* out[i] = x[idx[i]] for rows of C floats (ggml_get_rows on the hidden state, :1995) */
+NEXTERA_API int nxk_gather_rows(const float * x, int C, const int32_t * idx, int n, float * out, void * stream);
+/* ggml_mul_mat (:1140-1142) on a weight off the int8 path, in GGUF blocks of `type`
+ * (F32 F16 BF16 Q4_0 Q4_1 Q5_0 Q5_1 Q8_0 Q2_K Q3_K Q4_K Q5_K Q6_K):
+ * out[m][n] = W[n] . x[m] (+ bias[n]) for N weight rows of K inputs and M rows of x,
+ * with x first converted to the type's vec_dot type as ggml's CPU backend does
+ * (Q8_K / Q8_0 / Q8_1 codes, or F16 / BF16 rounding).  `workspace` holds the
+ * converted rows: nxk_mul_mat_workspace(type, K, M) bytes (0 = unsupported type).
+ * K must be a multiple of 32 (256 for the K-quants); N <= 524280. */
+NEXTERA_API size_t nxk_mul_mat_workspace(int type, int K, int M);
+NEXTERA_API int nxk_mul_mat(int type, const void * w, int N, int K, const float * x, int M, const float * bias,
+                            void * workspace, float * out, void * stream);
+
 /* ---- attention: op_attention (:785-852), varlen GQA over packed documents ----
  * half < 0: full attention inside each document, else the band |i - j| <= half.
  * scale[n_docs] on the device.  h_doc_start / h_doc_len: the same layout in host

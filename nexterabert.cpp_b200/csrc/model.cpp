@@ -121,6 +121,9 @@ struct nextera_context {
     // forward arena
     DevBuf X, X2, U, Fa, Fb, Fc, Q1, Q1s, Q2, Q2s;
     DevBuf meta, attn_ws, pooled;
+    // heads: gathered / pooled rows, their codes and scales, the transform's output, the
+    // mul_mat workspace and the head's output
+    DevBuf head_x, head_q, head_qs, head_y, head_ws, head_out, head_idx;
     int64_t cap_T = 0, cap_docs = 0;
     // host staging (pinned)
     void * h_stage = nullptr;
@@ -411,7 +414,11 @@ struct nextera_context * nextera_load(const char * path, struct nextera_params p
             weight_bytes += (size_t) w.n_in * w.n_out + sizeof(float) * (size_t) n_blk * w.n_out;
             continue;
         }
-        if (embedding) {
+        // head matrices off the int8 path (the classifier, float head weights) run on ggml_mul_mat in
+        // the reference (:1140-1142) and are kept in their file layout, like the embedding tables
+        const bool head_matrix = t.name == "classifier.weight" || t.name == "pooler.dense.weight" ||
+                                 t.name == "head.dense.weight" || t.name == "mlm.dense.weight";
+        if (embedding || head_matrix) {
             RawTensor & r = c->raw[t.name];
             r.type = t.type;
             memcpy(r.ne, t.ne, sizeof(r.ne));
@@ -1132,6 +1139,131 @@ int32_t encode_host(nextera_context * c, const int32_t * tokens, const int32_t *
     return rc;
 }
 
+// y = W x (+ bias) for M rows of x (K floats each) into out (M rows of W's n_out): the int8 linear
+// when W is on the int8 path (x quantized first, as the qcache's op_copy does, :1125-1130), else
+// ggml_mul_mat on W's blocks (:1140-1142).  Returns W's n_out, or 0 after printing why.
+int head_linear(nextera_context & c, Forward & fw, const std::string & name, const float * x, int M, int K,
+                const float * bias, float * out, cudaStream_t s) {
+    auto it = c.i8.find(name);
+    if (it != c.i8.end()) {
+        const I8Weight & w = it->second;
+        if (w.n_in != K || bias) {
+            fprintf(stderr, "nexterabert: '%s' cannot run on the int8 path here (%s)\n", name.c_str(),
+                    bias ? "a biased int8 linear" : "input width");
+            return 0;
+        }
+        const int nb = (K + I8_BLOCK - 1) / I8_BLOCK;
+        if (!c.head_q.reserve((size_t) M * K) || !c.head_qs.reserve(sizeof(float) * (size_t) (M + 3) / 4 * 4 * nb)) {
+            fprintf(stderr, "nexterabert: failed to allocate the head's buffers\n");
+            return 0;
+        }
+        fw.mark(PROF_ROWS);
+        fw.rows(nxk_quantize(x, M, K, c.head_q.as<int8_t>(), c.head_qs.as<float>(), s), "quantize");
+        fw.linear(name, c.head_q.as<int8_t>(), c.head_qs.as<float>(), M, nullptr, out);
+        return fw.ok ? w.n_out : 0;
+    }
+    auto rt = c.raw.find(name);
+    if (rt == c.raw.end()) {
+        fprintf(stderr, "nexterabert: missing tensor '%s'\n", name.c_str());
+        return 0;
+    }
+    const RawTensor & r = rt->second;
+    const size_t ws = nxk_mul_mat_workspace(r.type, K, M);
+    if (r.ne[0] != K || ws == 0) {
+        fprintf(stderr, "nexterabert: '%s' (type %d, %lld inputs) cannot multiply rows of %d\n", name.c_str(), r.type,
+                (long long) r.ne[0], K);
+        return 0;
+    }
+    if (!c.head_ws.reserve(ws)) {
+        fprintf(stderr, "nexterabert: failed to allocate the head's buffers\n");
+        return 0;
+    }
+    fw.mark(PROF_ROWS);
+    fw.rows(nxk_mul_mat(r.type, r.d.p, (int) r.ne[1], K, x, M, bias, c.head_ws.p, out, s), name.c_str(), 2);
+    return fw.ok ? (int) r.ne[1] : 0;
+}
+
+// transform(pre, x) (:1296-1301): dense (no bias) -> GELU(erf) -> ggml_norm * norm.weight, on M rows
+// of C floats; the result in c.head_y (M rows of C)
+float * head_transform(nextera_context & c, Forward & fw, const std::string & pre, const float * x, int M,
+                       cudaStream_t s) {
+    const int C = c.hp.n_embd;
+    if (!c.head_y.reserve(sizeof(float) * (size_t) M * C)) {
+        fprintf(stderr, "nexterabert: failed to allocate the head's buffers\n");
+        return nullptr;
+    }
+    float * y = c.head_y.as<float>();
+    const int n = head_linear(c, fw, pre + "dense.weight", x, M, C, nullptr, y, s);
+    if (n != C) {
+        if (n) fprintf(stderr, "nexterabert: '%sdense.weight' has %d outputs, not %d\n", pre.c_str(), n, C);
+        return nullptr;
+    }
+    fw.mark(PROF_ROWS);
+    fw.rows(nxk_gelu_norm(y, fw.p(pre + "norm.weight"), c.hp.ln_eps, M, C, y, s), "gelu_norm");
+    return fw.ok ? y : nullptr;
+}
+
+// copies a head's output to the host, waits, and reports device errors (as encode_host)
+int32_t finish_head(nextera_context & c, const float * d_out, size_t n, float * out,
+                    std::chrono::steady_clock::time_point t0) {
+    cudaMemcpyAsync(out, d_out, sizeof(float) * n, cudaMemcpyDeviceToHost, c.stream);
+    int32_t rc = 0;
+    if (cudaStreamSynchronize(c.stream) != cudaSuccess) {
+        fprintf(stderr, "nexterabert: device error: %s\n", cudaGetErrorString(cudaGetLastError()));
+        rc = 3;
+    } else if (int32_t e = nxk_take_error(c.stream)) {
+        fprintf(stderr, "nexterabert: a kernel timed out waiting on its pipeline (code 0x%x)\n", e);
+        rc = 3;
+    }
+    collect_profile(c);
+    c.last_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    if (c.prof.enabled) {
+        c.prof.total_ms += c.last_ms;
+        c.prof.calls++;
+    }
+    return rc;
+}
+
+enum head_kind { HEAD_POOLER, HEAD_CLASSIFIER };
+
+// run_forward with a head (:1866-1925): the encoder, then pooler (:1304-1310) or classifier (:1313-1317)
+int32_t run_head(nextera_context * c, const int32_t * tokens, const int32_t * types, const int32_t * lengths,
+                 int32_t n_seqs, head_kind head, float * out) {
+    const auto t0 = std::chrono::steady_clock::now();
+    cudaSetDevice(c->device);
+    if (!tokens || !out) return 1;
+    Batch b;
+    float rope0 = 0.0f;
+    int rc = prepare(*c, tokens, types, lengths, n_seqs, true, b, rope0);
+    if (rc) return rc;
+    const hparams & hp = c->hp;
+    const int C = hp.n_embd;
+    const bool pooled = head == HEAD_POOLER || hp.cls == CLS_SEQUENCE || hp.cls == CLS_CHOICE;
+    // the encoder's per-document pooling with the 1/n scale is op_doc_mean (:662-674)
+    float * hid = nullptr;
+    rc = run_encoder(*c, b, rope0, tokens, types, true, c->stream, nullptr, nullptr, 0, &hid);
+    if (rc) return rc;
+    Forward fw(*c, c->stream);
+    const int M = pooled ? b.n_docs : b.T;
+    float * h = head_transform(*c, fw, pooled ? "pooler." : "head.", pooled ? c->pooled.as<float>() : hid, M,
+                               c->stream);
+    if (!h) return fw.ok ? 2 : 3;
+    if (head == HEAD_POOLER) {
+        fw.mark(-1);
+        return finish_head(*c, h, (size_t) M * C, out, t0);
+    }
+    const int L = hp.n_labels;
+    if (!c->head_out.reserve(sizeof(float) * (size_t) M * std::max(L, 1))) return 2;
+    const int n = head_linear(*c, fw, "classifier.weight", h, M, C, fw.p("classifier.bias"), c->head_out.as<float>(),
+                              c->stream);
+    fw.mark(-1);
+    if (n != L) {
+        if (n) fprintf(stderr, "nexterabert: the classifier has %d outputs for %d labels\n", n, L);
+        return 3;
+    }
+    return finish_head(*c, c->head_out.as<float>(), (size_t) M * L, out, t0);
+}
+
 } // namespace
 
 int32_t nextera_encode(struct nextera_context * c, const int32_t * tokens, const int32_t * lengths, int32_t n_seqs,
@@ -1247,31 +1379,62 @@ int32_t nextera_encode_sharded(struct nextera_context * c, const int32_t * d_tok
                        &hid, &sh);
 }
 
-int32_t nextera_pooler_output(struct nextera_context * c, const int32_t *, const int32_t *, const int32_t *, int32_t,
-                              float *) {
+int32_t nextera_pooler_output(struct nextera_context * c, const int32_t * tokens, const int32_t * token_types,
+                              const int32_t * lengths, int32_t n_seqs, float * out) {
     if (!c->hp.has_pooler) {
         fprintf(stderr, "nexterabert: this file has no pooler\n");
         return 1;
     }
-    fprintf(stderr, "nexterabert: pooler_output is not available on the GPU path of this build\n");
-    return 1;
+    return run_head(c, tokens, token_types, lengths, n_seqs, HEAD_POOLER, out);
 }
 
-int32_t nextera_classify(struct nextera_context * c, const int32_t *, const int32_t *, const int32_t *, int32_t,
-                         float *) {
+int32_t nextera_classify(struct nextera_context * c, const int32_t * tokens, const int32_t * token_types,
+                         const int32_t * lengths, int32_t n_seqs, float * logits) {
     if (c->hp.cls == CLS_NONE) {
         fprintf(stderr, "nexterabert: this file has no classifier head\n");
         return 1;
     }
-    fprintf(stderr, "nexterabert: classify is not available on the GPU path of this build\n");
-    return 1;
+    return run_head(c, tokens, token_types, lengths, n_seqs, HEAD_CLASSIFIER, logits);
 }
 
-int32_t nextera_mlm_logits(struct nextera_context * c, const int32_t *, int32_t, const int32_t *, int32_t, float *) {
+// nextera_mlm_logits (:1963-2011): one sequence; transform("mlm.") of the selected rows, then the
+// decoder (the embedding table, or mlm.decoder.weight when untied) plus mlm.bias
+int32_t nextera_mlm_logits(struct nextera_context * c, const int32_t * tokens, int32_t n_tokens,
+                           const int32_t * positions, int32_t n_pos, float * logits) {
+    const auto t0 = std::chrono::steady_clock::now();
     if (!c->hp.has_mlm) {
         fprintf(stderr, "nexterabert: this file has no MLM head\n");
         return 1;
     }
-    fprintf(stderr, "nexterabert: mlm_logits is not available on the GPU path of this build\n");
-    return 1;
+    if (n_pos <= 0 || !tokens || !positions || !logits) return 1;
+    cudaSetDevice(c->device);
+    Batch b;
+    float rope0 = 0.0f;
+    int rc = prepare(*c, tokens, nullptr, &n_tokens, 1, true, b, rope0);
+    if (rc) return rc;
+    for (int32_t i = 0; i < n_pos; ++i) {
+        if (positions[i] < 0 || positions[i] >= n_tokens) return 1;
+    }
+    const hparams & hp = c->hp;
+    const int C = hp.n_embd;
+    float * hid = nullptr;
+    rc = run_encoder(*c, b, rope0, tokens, nullptr, true, c->stream, nullptr, nullptr, 0, &hid);
+    if (rc) return rc;
+    if (!c->head_idx.reserve(sizeof(int32_t) * (size_t) n_pos) || !c->head_x.reserve(sizeof(float) * (size_t) n_pos * C) ||
+        !c->head_out.reserve(sizeof(float) * (size_t) n_pos * hp.n_vocab))
+        return 2;
+    Forward fw(*c, c->stream);
+    cudaMemcpyAsync(c->head_idx.p, positions, sizeof(int32_t) * (size_t) n_pos, cudaMemcpyHostToDevice, c->stream);
+    fw.mark(PROF_ROWS);
+    fw.rows(nxk_gather_rows(hid, C, c->head_idx.as<int32_t>(), n_pos, c->head_x.as<float>(), c->stream), "get_rows");
+    float * h = fw.ok ? head_transform(*c, fw, "mlm.", c->head_x.as<float>(), n_pos, c->stream) : nullptr;
+    if (!h) return fw.ok ? 2 : 3;
+    const std::string dec = c->raw.count("mlm.decoder.weight") ? "mlm.decoder.weight" : "embedding.weight";
+    const int n = head_linear(*c, fw, dec, h, n_pos, C, fw.p("mlm.bias"), c->head_out.as<float>(), c->stream);
+    fw.mark(-1);
+    if (n != hp.n_vocab) {
+        if (n) fprintf(stderr, "nexterabert: the MLM decoder has %d outputs for %d tokens\n", n, hp.n_vocab);
+        return 3;
+    }
+    return finish_head(*c, c->head_out.as<float>(), (size_t) n_pos * hp.n_vocab, logits, t0);
 }

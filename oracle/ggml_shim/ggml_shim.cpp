@@ -5,7 +5,8 @@
 // What the reference delegates to ggml is restated here, not taken from ggml
 // (which is not available): block dequantization (oracle/dequant.c, pinned
 // against gguf-py), get_rows, add / mul with row broadcast, LayerNorm
-// (mean / variance in double), a plain fp32 mul_mat and GELU(erf).  The graph
+// (mean / variance in double), mul_mat with ggml's activation conversion to the
+// weight's vec_dot type (oracle/vecdot.c) and GELU(erf).  The graph
 // runs its nodes in order; each custom op is called as fn(dst, ith, nth, ud) on
 // every thread of the pool, exactly as the reference expects.
 #include "ggml.h"
@@ -395,28 +396,29 @@ static void compute_node(ggml_backend * be, ggml_tensor * t) {
             return;
         }
         case SHIM_OP_MUL_MAT: {
+            // ggml's CPU mul_mat: the activation row goes to the weight type's vec_dot
+            // type first (Q8_K / Q8_0 / Q8_1 / F16 ...), then one dot per weight row
+            // (oracle/vecdot.c)
             const ggml_tensor * a = t->src[0], * b = t->src[1];
             const int64_t K = a->ne[0], N = a->ne[1], M = b->ne[1];
             const size_t rs = ggml_row_size(a->type, K);
+            const size_t ab = or_act_bytes((int) a->type, K);
+            GGML_ASSERT(ab > 0);
+            std::vector<uint8_t> act(ab * (size_t) M);
+            parallel_rows(tp, M, [&](int64_t m) {
+                GGML_ASSERT(or_quantize_act((int) a->type, (const float *) b->data + m * K, K, act.data() + ab * m) == 0);
+            });
             parallel_rows(tp, N, [&](int64_t n) {
-                std::vector<float> w((size_t) K);
-                or_dequant_row((int) a->type, (const uint8_t *) a->data + rs * (size_t) n, w.data(), K);
+                const uint8_t * wr = (const uint8_t *) a->data + rs * (size_t) n;
                 for (int64_t m = 0; m < M; ++m) {
-                    const float * x = (const float *) b->data + m * K;
-                    float s = 0.0f;
-                    for (int64_t k = 0; k < K; ++k) s += w[(size_t) k] * x[k];
-                    ((float *) t->data)[m * N + n] = s;
+                    ((float *) t->data)[m * N + n] = or_vec_dot((int) a->type, wr, act.data() + ab * m, K);
                 }
             });
             return;
         }
         case SHIM_OP_GELU_ERF: {
             const ggml_tensor * a = t->src[0];
-            const int64_t n = t->ne[0] * t->ne[1] * t->ne[2] * t->ne[3];
-            for (int64_t i = 0; i < n; ++i) {
-                const float x = ((const float *) a->data)[i];
-                ((float *) t->data)[i] = 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
-            }
+            or_gelu_erf((const float *) a->data, t->ne[0] * t->ne[1] * t->ne[2] * t->ne[3], (float *) t->data);
             return;
         }
     }

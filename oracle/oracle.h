@@ -87,6 +87,16 @@ void or_pool(const float * hidden, const int32_t * lengths, int n_seqs, int C, i
 /* rope table (build_rope :1322-1338) */
 void or_rope_table(int n_pos, float base, int head_dim, float * cos_t, float * sin_t);
 
+/* ---- ggml_mul_mat on a weight off the int8 path (vecdot.c; ggml restated, unpinned) ---- */
+uint16_t or_fp32_to_fp16(float f);
+int    or_vec_dot_family(int type);
+size_t or_act_bytes(int type, int64_t K);
+int    or_quantize_act(int type, const float * x, int64_t K, void * out);
+float  or_vec_dot(int type, const void * wrow, const void * xact, int64_t K);
+int    or_mul_mat(int type, const void * w, int64_t N, int64_t K, const float * x, int64_t M, float * out);
+/* GELU(erf) as ggml_gelu_erf: 0.5 x (1 + erf(x / sqrt 2)) */
+void   or_gelu_erf(const float * x, int64_t n, float * out);
+
 /* ---- whole encoder (builder::encoder :1271-1294 + run_forward) ---- */
 typedef struct or_model or_model;
 or_model * or_load(const char * path);

@@ -74,6 +74,20 @@ class HParams:
     sep_id: int = 50282
     pad_id: int = 50283
     mask_id: int = 50284
+    # heads (python/convert_hf_to_gguf.py:39-66, :125-166): a classifier task
+    # ("sequence-classification", "multiple-choice", "token-classification",
+    # "question-answering") with n_labels outputs; a pooler kept without one;
+    # an untied MLM decoder; a classifier written by an f16 conversion
+    cls_task: str = ""
+    n_labels: int = 0
+    pooler: bool = False
+    untied_decoder: bool = False
+    cls_f16: bool = False
+
+
+# fields added after the first fixtures: left out of the cache key at their defaults
+_LATE_FIELDS = {"cls_task": "", "n_labels": 0, "pooler": False, "untied_decoder": False, "cls_f16": False}
+POOLED_TASKS = ("sequence-classification", "multiple-choice")
 
 
 # 8 lily, 6 swa, 2 attn, 2 hra: the published block mix (141 int8 linears with mlm.dense).
@@ -259,6 +273,14 @@ def tensor_specs(hp: HParams):
     if hp.mlm_head:
         out += [("mlm.dense.weight", (C, C), "w"), ("mlm.norm.weight", (C,), "gain"),
                 ("mlm.bias", (hp.n_vocab,), "bias")]
+        if hp.untied_decoder:
+            out += [("mlm.decoder.weight", (hp.n_vocab, C), "w")]
+    if hp.cls_task in POOLED_TASKS or hp.pooler:
+        out += [("pooler.dense.weight", (C, C), "w"), ("pooler.norm.weight", (C,), "gain")]
+    if hp.cls_task and hp.cls_task not in POOLED_TASKS:
+        out += [("head.dense.weight", (C, C), "w"), ("head.norm.weight", (C,), "gain")]
+    if hp.cls_task:
+        out += [("classifier.weight", (hp.n_labels, C), "w"), ("classifier.bias", (hp.n_labels,), "bias")]
     return out
 
 
@@ -281,10 +303,14 @@ def _small_params(kind: str, shape, rng: np.random.Generator) -> np.ndarray:
     raise ValueError(kind)
 
 
-def tensor_type(name: str, shape, preset: str):
+def tensor_type(name: str, shape, preset: str, cls_f16: bool = False):
     """Storage type of one tensor under `preset` (quantize.cpp:195-206)."""
     base, more = PRESETS[preset]
-    is_matrix = (len(shape) == 2 and name.endswith(".weight") and name != "classifier.weight"
+    if name == "classifier.weight":
+        # the quantizer keeps it as converted (quantize.cpp:171-175); the converter writes a
+        # matrix with both dims >= 32 as f16 under --outtype f16 (convert_hf_to_gguf.py:216-218)
+        return QT.F16 if (cls_f16 or preset == "F16") and min(shape) >= 32 else QT.F32
+    is_matrix = (len(shape) == 2 and name.endswith(".weight")
                  and shape[1] >= 32 and shape[0] >= 32)
     if not is_matrix:
         return QT.F32
@@ -321,6 +347,9 @@ def write_model(path: str | os.PathLike, hp: HParams, preset: str, seed: int = 0
     w.add_float32(k + "rms_norm_epsilon", 1e-8)
     w.add_float32(k + "layer_norm_epsilon", 1e-5)
     w.add_bool(k + "mlm_head", hp.mlm_head)
+    if hp.cls_task:
+        w.add_string(k + "classifier.task", hp.cls_task)
+        w.add_array(k + "classifier.labels", [f"LABEL_{i}" for i in range(hp.n_labels)])
     w.add_uint32("tokenizer.ggml.cls_token_id", hp.cls_id)
     w.add_uint32("tokenizer.ggml.seperator_token_id", hp.sep_id)
     w.add_uint32("tokenizer.ggml.padding_token_id", hp.pad_id)
@@ -330,7 +359,7 @@ def write_model(path: str | os.PathLike, hp: HParams, preset: str, seed: int = 0
             arr = (0.02 * rng.standard_normal(shape)).astype(np.float32)
         else:
             arr = _small_params(kind, shape, rng)
-        qt = tensor_type(name, shape, preset)
+        qt = tensor_type(name, shape, preset, hp.cls_f16)
         if qt == QT.F32:
             w.add_tensor(name, np.ascontiguousarray(arr))
         elif qt == QT.F16:
@@ -354,7 +383,11 @@ def model_cache_dir() -> Path:
 
 def cached_model(name: str, hp: HParams, preset: str, seed: int = 0) -> Path:
     """Path of a generated model, written on first use (the key covers every setting)."""
-    key = json.dumps({"hp": asdict(hp), "preset": preset, "seed": seed, "v": 1}, sort_keys=True)
+    d = asdict(hp)
+    for k, v in _LATE_FIELDS.items():
+        if d.get(k) == v:
+            del d[k]
+    key = json.dumps({"hp": d, "preset": preset, "seed": seed, "v": 1}, sort_keys=True)
     h = hashlib.sha256(key.encode()).hexdigest()[:12]
     p = model_cache_dir() / f"{name}-{preset}-{h}.gguf"
     if not p.exists():

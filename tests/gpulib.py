@@ -67,6 +67,10 @@ def load_lib(path=None):
         "nxk_attention_workspace": ([i32p, c_int, c_int], c_size),
         "nxk_attention": ([vp, vp, vp, c_int, c_int, c_int, c_int, c_int, vp, vp, vp, vp, c_int, i32p, i32p,
                            vp, c_size, vp, vp], c_int),
+        "nxk_gelu_norm": ([vp, vp, c_float, c_int, c_int, vp, vp], c_int),
+        "nxk_gather_rows": ([vp, c_int, vp, c_int, vp, vp], c_int),
+        "nxk_mul_mat_workspace": ([c_int, c_int, c_int], c_size),
+        "nxk_mul_mat": ([c_int, vp, c_int, c_int, vp, c_int, vp, vp, vp, vp], c_int),
         "nextera_default_params": ([], Params),
         "nextera_load": ([ctypes.c_char_p, Params], vp),
         "nextera_free": ([vp], None),
@@ -78,6 +82,13 @@ def load_lib(path=None):
                                     ctypes.c_int32),
         "nextera_encode_device": ([vp, vp, vp, i32p, ctypes.c_int32, vp, vp, ctypes.c_int32, vp], ctypes.c_int32),
         "nextera_system_info": ([vp], ctypes.c_char_p),
+        "nextera_n_labels": ([vp], ctypes.c_int32),
+        "nextera_has_pooler": ([vp], ctypes.c_int32),
+        "nextera_has_mlm_head": ([vp], ctypes.c_int32),
+        "nextera_classifier_task": ([vp], ctypes.c_char_p),
+        "nextera_pooler_output": ([vp, i32p, i32p, i32p, ctypes.c_int32, f32p], ctypes.c_int32),
+        "nextera_classify": ([vp, i32p, i32p, i32p, ctypes.c_int32, f32p], ctypes.c_int32),
+        "nextera_mlm_logits": ([vp, i32p, ctypes.c_int32, i32p, ctypes.c_int32, f32p], ctypes.c_int32),
         "nextera_ftype": ([vp], ctypes.c_char_p),
         "nextera_last_ms": ([vp], ctypes.c_double),
         "nextera_debug_set_layers": ([vp, ctypes.c_int32], None),

@@ -109,6 +109,11 @@ class Oracle:
         L.or_pool.argtypes = [f32p, i32p, c_int, c_int, c_int, f32p]
         L.or_rope_table.argtypes = [c_int, c_float, c_int, f32p, f32p]
         L.or_set_threads.argtypes = [c_int]
+        L.or_act_bytes.restype = ctypes.c_size_t
+        L.or_act_bytes.argtypes = [c_int, ctypes.c_int64]
+        L.or_quantize_act.argtypes = [c_int, f32p, ctypes.c_int64, vp]
+        L.or_mul_mat.argtypes = [c_int, vp, ctypes.c_int64, ctypes.c_int64, f32p, ctypes.c_int64, f32p]
+        L.or_gelu_erf.argtypes = [f32p, ctypes.c_int64, f32p]
 
     # -- ops -----------------------------------------------------------------
     def dequant_row(self, qtype: int, data: np.ndarray, n: int) -> np.ndarray:
@@ -230,6 +235,31 @@ class Oracle:
                             ptr(rd), ptr(start), ptr(ln), ptr(out))
         return out
 
+    def act_bytes(self, qtype: int, K: int) -> int:
+        return int(self.L.or_act_bytes(qtype, K))
+
+    def quantize_act(self, qtype: int, x: np.ndarray) -> np.ndarray:
+        """Rows of x in the weight type's vec_dot type (oracle/vecdot.c layout), one row per line."""
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, x.shape[-1])
+        K = x.shape[1]
+        out = np.zeros((x.shape[0], self.act_bytes(qtype, K)), np.uint8)
+        for m in range(x.shape[0]):
+            assert self.L.or_quantize_act(qtype, ptr(x[m]), K, out[m].ctypes.data) == 0
+        return out
+
+    def mul_mat(self, qtype: int, w: np.ndarray, N: int, K: int, x: np.ndarray) -> np.ndarray:
+        """ggml_mul_mat: out[m][n] = W[n] . x[m], W in GGUF blocks of qtype."""
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty((x.shape[0], N), np.float32)
+        assert self.L.or_mul_mat(qtype, np.ascontiguousarray(w).ctypes.data, N, K, ptr(x), x.shape[0], ptr(out)) == 0
+        return out
+
+    def gelu_erf(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty_like(x)
+        self.L.or_gelu_erf(ptr(x), x.size, ptr(out))
+        return out
+
     def layer_norm(self, x, w, b, eps):
         out = np.empty_like(x)
         self.L.or_layer_norm(ptr(x), ptr(w), ptr(b), eps, x.shape[0], x.shape[1], ptr(out))
@@ -336,6 +366,13 @@ class RefLib:
         L.nextera_last_ms.restype = ctypes.c_double
         L.nextera_system_info.argtypes = [vp]
         L.nextera_system_info.restype = ctypes.c_char_p
+        L.nextera_n_vocab.argtypes = [vp]
+        L.nextera_n_labels.argtypes = [vp]
+        L.nextera_classifier_task.argtypes = [vp]
+        L.nextera_classifier_task.restype = ctypes.c_char_p
+        L.nextera_pooler_output.argtypes = [vp, i32p, i32p, i32p, c_int, f32p]
+        L.nextera_classify.argtypes = [vp, i32p, i32p, i32p, c_int, f32p]
+        L.nextera_mlm_logits.argtypes = [vp, i32p, c_int, i32p, c_int, f32p]
 
     @staticmethod
     def _q(T, C, quant):
@@ -468,3 +505,35 @@ class RefLib:
         if rc != 0:
             raise RuntimeError(f"reference encode failed ({rc})")
         return hid, pooled
+
+    # -- heads (nextera_pooler_output / nextera_classify / nextera_mlm_logits) --
+    def pooler_output(self, h, tokens, lengths, types=None):
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        lengths = np.ascontiguousarray(lengths, np.int32)
+        types = None if types is None else np.ascontiguousarray(types, np.int32)
+        out = np.empty((len(lengths), self.L.nextera_n_embd(h)), np.float32)
+        rc = self.L.nextera_pooler_output(h, ptr(tokens), ptr(types), ptr(lengths), len(lengths), ptr(out))
+        if rc != 0:
+            raise RuntimeError(f"reference pooler_output failed ({rc})")
+        return out
+
+    def classify(self, h, tokens, lengths, types=None):
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        lengths = np.ascontiguousarray(lengths, np.int32)
+        types = None if types is None else np.ascontiguousarray(types, np.int32)
+        task = self.L.nextera_classifier_task(h).decode()
+        rows = len(lengths) if task in ("sequence-classification", "multiple-choice") else int(lengths.sum())
+        out = np.empty((rows, self.L.nextera_n_labels(h)), np.float32)
+        rc = self.L.nextera_classify(h, ptr(tokens), ptr(types), ptr(lengths), len(lengths), ptr(out))
+        if rc != 0:
+            raise RuntimeError(f"reference classify failed ({rc})")
+        return out
+
+    def mlm_logits(self, h, tokens, positions):
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        positions = np.ascontiguousarray(positions, np.int32)
+        out = np.empty((len(positions), self.L.nextera_n_vocab(h)), np.float32)
+        rc = self.L.nextera_mlm_logits(h, ptr(tokens), len(tokens), ptr(positions), len(positions), ptr(out))
+        if rc != 0:
+            raise RuntimeError(f"reference mlm_logits failed ({rc})")
+        return out
