@@ -369,6 +369,18 @@ def run_reference(args, rank, world, dist):
     emit(line)
 
 
+def hbm_peak():
+    """(GB/s, source): the driver-measured copy bandwidth, else the earlier measurement on this pool."""
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        pass
+    if "hbm_gbs" in peaks:
+        return float(peaks["hbm_gbs"]), "MEASURED_PEAKS.json hbm_gbs (of measured)"
+    return 6650.0, "6650 GB/s, an earlier copy measurement on this pool (of fallback: MEASURED_PEAKS.json absent)"
+
+
 def int8_peak_tops(torch) -> float:
     """Measured dense int8 throughput of the library GEMM (cuBLASLt via torch._int_mm), TOPS."""
     n = 8192
@@ -505,14 +517,7 @@ def run_b200(args, rank, world, local_rank, dist):
     k_ms = {"int8_linear": kind[0], "attention": kind[1], "row_ops": kind[2]}
     dev_ms = sum(k_ms.values())
     shares = {k: v / dev_ms for k, v in k_ms.items()}
-    peaks = {}
-    try:
-        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
-    except (OSError, ValueError):
-        pass
-    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
-    hbm_src = ("MEASURED_PEAKS.json hbm_gbs (of measured)" if "hbm_gbs" in peaks
-               else "6650 GB/s, an earlier copy measurement on this pool (of fallback: MEASURED_PEAKS.json absent)")
+    hbm_pk, hbm_src = hbm_peak()
     lin_ops = linear_ops(lengths)
     att_flops, att_bytes = attention_work(lengths)
     top = max(k_ms, key=k_ms.get)
@@ -532,13 +537,13 @@ def run_b200(args, rank, world, local_rank, dist):
                "peak_source": "fp32 FMA throughput measured in this run (cuBLAS SGEMM, TF32 off, 8192^3)",
                "algorithmic": "2 * 64 multiply-adds per (query, head, key) for the scores and again for the "
                               "weighted values, keys in each query's range",
-               "hbm_gbs": att_bytes / (k_ms["attention"] * 1e-3) / 1e9, "hbm_peak_gbs": hbm_peak,
+               "hbm_gbs": att_bytes / (k_ms["attention"] * 1e-3) / 1e9, "hbm_peak_gbs": hbm_pk,
                "hbm_peak_source": hbm_src,
                "hbm_algorithmic": "q + k + v read, output written once per attention layer (fp32)"}
         att["frac"] = att["achieved"] / att["peak"]
         roof = lin if top == "int8_linear" else att if top == "attention" else None
         if roof is None:
-            roof = {"bound": "hbm", "achieved": None, "peak": hbm_peak, "unit": "GB/s", "frac": None,
+            roof = {"bound": "hbm", "achieved": None, "peak": hbm_pk, "unit": "GB/s", "frac": None,
                     "kernel": "row ops", "peak_source": hbm_src}
         tf = ROOT / "profiles" / "traffic.json"
         roof["traffic"] = None
@@ -567,6 +572,143 @@ def run_b200(args, rank, world, local_rank, dist):
         emit(line)
 
 
+HEADS_METRIC = "classified documents/s (mixed-length batch, sequence classification, Q4_K_M)"
+
+
+def run_heads(args):
+    """--heads (one GPU): the task heads on the full-size model with a 2-label sequence classifier.
+
+    * classify: nextera_classify over the config-4 batch (host API, wall clock around each call,
+      which returns after the logits are on the host), beside nextera_encode on the same batch;
+    * mlm_logits: fill-mask shape, one 512-token sequence with 77 masked positions (host API);
+    * the decoder alone: nxk_mul_mat over the 50368 x 1024 Q4_K embedding table for 8, 77 and 512
+      rows, CUDA events on the launching stream, against the HBM peak (table bytes + output);
+    * the reference (oracle/_ref) on the host cores for mlm_logits of the same shape."""
+    import torch
+    import heads_util as hu
+    import synth_model as sm
+    from gpulib import load_lib
+
+    torch.cuda.set_device(0)
+    L = load_lib()
+    hp = sm.full_hparams(cls_task="sequence-classification", n_labels=2)
+    path = sm.cached_model("full_cls", hp, args.preset, seed=0)
+    tokens, lengths = workload(0, args.docs)
+    T, n_docs = int(lengths.sum()), len(lengths)
+    h = L.nextera_load(str(path).encode(), L.nextera_default_params())
+    assert h, "nextera_load failed"
+    i32 = ctypes.POINTER(ctypes.c_int32)
+    f32 = ctypes.POINTER(ctypes.c_float)
+    tok = np.ascontiguousarray(tokens, np.int32)
+    lens = np.ascontiguousarray(lengths, np.int32)
+    logits = np.empty((n_docs, 2), np.float32)
+    pooled = np.empty((n_docs, 1024), np.float32)
+
+    def wall(fn, steps, warmup):
+        for _ in range(warmup):
+            fn()
+        ts = []
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return sum(ts) / len(ts)
+
+    def classify():
+        assert L.nextera_classify(h, tok.ctypes.data_as(i32), None, lens.ctypes.data_as(i32), n_docs,
+                                  logits.ctypes.data_as(f32)) == 0
+
+    def encode():
+        assert L.nextera_encode(h, tok.ctypes.data_as(i32), lens.ctypes.data_as(i32), n_docs, None,
+                                pooled.ctypes.data_as(f32), 1) == 0
+
+    t_cls = wall(classify, args.steps, args.warmup)
+    t_enc = wall(encode, args.steps, args.warmup)
+    log(f"classify {t_cls * 1e3:.1f} ms, encode {t_enc * 1e3:.1f} ms per batch")
+
+    seq = sm.random_tokens(512, hp.n_vocab, seed=77)
+    pos = np.ascontiguousarray(np.sort(np.random.default_rng(78).choice(512, 77, replace=False)), np.int32)
+    ml = np.empty((77, hp.n_vocab), np.float32)
+
+    def mlm():
+        assert L.nextera_mlm_logits(h, seq.ctypes.data_as(i32), 512, pos.ctypes.data_as(i32), 77,
+                                    ml.ctypes.data_as(f32)) == 0
+
+    t_mlm = wall(mlm, 10, 3)
+    L.nextera_free(h)
+
+    # the decoder kernel alone
+    typ, table, ne0, ne1 = hu.raw_tensor(path, "embedding.weight")
+    d_tab = torch.from_numpy(np.ascontiguousarray(table)).cuda()
+    stream = torch.cuda.current_stream()
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+    peak, peak_src = hbm_peak()
+    dec = []
+    for M in (8, 77, 512):
+        x = torch.randn((M, ne0), dtype=torch.float32, device="cuda")
+        ws = torch.empty(L.nxk_mul_mat_workspace(typ, ne0, M), dtype=torch.uint8, device="cuda")
+        out = torch.empty((M, ne1), dtype=torch.float32, device="cuda")
+
+        def launch(sp):
+            assert L.nxk_mul_mat(typ, ctypes.c_void_p(d_tab.data_ptr()), ne1, ne0, ctypes.c_void_p(x.data_ptr()),
+                                 M, None, ctypes.c_void_p(ws.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                                 sp) == 0
+        # 20 calls captured in a CUDA graph, so host launch overhead does not enter the time
+        gs = torch.cuda.Stream()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(gs):
+            gsp = ctypes.c_void_p(gs.cuda_stream)
+            for _ in range(3):
+                launch(gsp)
+            torch.cuda.synchronize()
+            with torch.cuda.graph(graph, stream=gs):
+                for _ in range(20):
+                    launch(gsp)
+        for _ in range(3):
+            graph.replay()
+        n = 10
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(n):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (20 * n)
+        byts = table.nbytes + 4.0 * M * ne1 + 4.0 * M * ne0
+        dec.append({"rows": M, "us": us, "bytes": byts, "gbs": byts / us * 1e-3, "frac_hbm": byts / us * 1e-3 / peak,
+                    "int_macs_per_s": M * ne1 * ne0 / (us * 1e-6)})
+        log(f"decoder M={M}: {us:.1f} us, {byts / us * 1e-3:.0f} GB/s")
+
+    # the reference on the host cores, same mlm_logits call
+    ref = None
+    if not args.no_cpu_baseline:
+        from oracle_lib import RefLib, ref_library_path
+        if ref_library_path() is not None:
+            r = RefLib()
+            cores = os.cpu_count() or 1
+            rh = r.load(path, cores)
+            r.mlm_logits(rh, seq, pos)
+            t0 = time.perf_counter()
+            r.mlm_logits(rh, seq, pos)
+            ref = {"ms": 1e3 * (time.perf_counter() - t0), "cores": cores, "kind": "reference"}
+            r.L.nextera_free(rh)
+
+    emit({"metric": HEADS_METRIC, "unit": "documents/s", "value": n_docs / t_cls, "n_gpus": 1,
+          "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": "int8+fp32",
+          "data": "synthetic (seeded lengths and ids; random-init weights N(0,0.02), Q4_K_M, 2-label classifier)",
+          "config": {"workload": f"cfg4 batch ({n_docs} docs, {T} tokens) through nextera_classify; "
+                                 "fill-mask: 512 tokens, 77 positions through nextera_mlm_logits",
+                     "model": "NexteraBERT-synthetic + pooler + classifier + tied MLM head"},
+          "classify": {"ms_per_batch": 1e3 * t_cls, "tokens_per_s": T / t_cls,
+                       "encode_ms_per_batch": 1e3 * t_enc, "head_overhead": t_cls / t_enc - 1.0,
+                       "api": "nextera_classify (host buffers, wall clock)"},
+          "mlm_logits": {"ms_per_call": 1e3 * t_mlm, "tokens": 512, "positions": 77,
+                         "api": "nextera_mlm_logits (host buffers, wall clock)", "reference": ref},
+          "decoder_kernel": {"type": "Q4_K", "table_bytes": int(table.nbytes), "launches": dec,
+                             "peak_hbm_gbs": peak, "peak_source": peak_src}})
+
+
 def main() -> int:
     global _RESULT_OUT
     sys.stdout.flush()
@@ -584,6 +726,7 @@ def main() -> int:
     ap.add_argument("--seq-len", type=int, default=65536, help="config 5 sequence length")
     ap.add_argument("--profile-run", action="store_true", help="one untimed step (for profilers)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--heads", action="store_true", help="time the task heads instead (one GPU)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -591,6 +734,9 @@ def main() -> int:
     dist = None
     if args.impl == "reference":
         run_reference(args, rank, world, dist)
+        return 0
+    if args.heads:
+        run_heads(args)
         return 0
     if world > 1:
         import datetime

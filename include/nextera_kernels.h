@@ -148,7 +148,8 @@ NEXTERA_API int nxk_gather_rows(const float * x, int C, const int32_t * idx, int
  * with x first converted to the type's vec_dot type as ggml's CPU backend does
  * (Q8_K / Q8_0 / Q8_1 codes, or F16 / BF16 rounding).  `workspace` holds the
  * converted rows: nxk_mul_mat_workspace(type, K, M) bytes (0 = unsupported type).
- * K must be a multiple of 32 (256 for the K-quants); N <= 524280. */
+ * K must be a multiple of 32 (256 for the K-quants); N <= 524280; w, x and workspace
+ * 16-byte aligned. */
 NEXTERA_API size_t nxk_mul_mat_workspace(int type, int K, int M);
 NEXTERA_API int nxk_mul_mat(int type, const void * w, int N, int K, const float * x, int M, const float * bias,
                             void * workspace, float * out, void * stream);

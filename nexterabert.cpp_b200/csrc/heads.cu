@@ -17,11 +17,11 @@
 // Both steps run here on the raw GGUF blocks: `act_prep_kernel` quantizes the
 // activation rows exactly as ggml does (every code and scale bit-identical),
 // and `mul_mat_kernel` decodes 32 weights per lane into packed int8 codes and
-// takes the integer dots with dp4a, so isum and msum are exact.  Only the fp32
-// sum of the per-block terms runs in another order than ggml's SIMD lanes.
+// takes each 32-weight chunk's integer dots with dp4a (exact).  From there the
+// arithmetic is fp32, in another order than ggml's SIMD lanes.
 //
-// The MLM decoder is HBM-bound for the usual handful of masked positions: the
-// table (29 MB at Q4_K for 50368 x 1024) is read once per tile of 8 positions.
+// The MLM decoder reads its table (29 MB at Q4_K for 50368 x 1024) once per
+// tile of 8 positions; four weight rows per warp share each activation load.
 #include "common.cuh"
 #include "dequant.cuh"
 #include "nextera_kernels.h"
@@ -173,7 +173,10 @@ __global__ void __launch_bounds__(256) act_prep_kernel(const float * __restrict_
 
 // ---------------------------------------------------------------------------
 // 32 weights of one row as packed int8 codes plus their integer sub-scales
-// (one per 16 weights) and sub-mins, and the block's fp32 d / dmin (or m)
+// (one per 16 weights) and sub-mins, and the block's fp32 d / dmin (or m).
+// Loads are as wide as the block layout allows: a row starts 16-byte aligned
+// and its blocks are 144 / 176 (16-aligned), 84 / 20 (4), 24 (8) or
+// 210 / 110 / 34 / 22 / 18 bytes (2-aligned).
 // ---------------------------------------------------------------------------
 struct Chunk {
     uint32_t q[8];
@@ -181,116 +184,176 @@ struct Chunk {
     float d, dm;
 };
 
-__device__ __forceinline__ void put(uint32_t (&q)[8], int e, int v) { q[e >> 2] |= (uint32_t) (v & 255) << (8 * (e & 3)); }
+__device__ __forceinline__ uint32_t ld16(const uint8_t * p) { return __ldg((const unsigned short *) p); }
+__device__ __forceinline__ uint32_t ld32(const uint8_t * p) { return __ldg((const unsigned int *) p); }
+__device__ __forceinline__ uint32_t ld32_2(const uint8_t * p) { return ld16(p) | (ld16(p + 2) << 16); }
+__device__ __forceinline__ float h2f(uint32_t h) { return __half2float(__ushort_as_half((unsigned short) (h & 0xffffu))); }
+
+// n 32-bit words from p, which is 16- / 4- / 2-byte aligned (ALIGN)
+template <int ALIGN, int NW>
+__device__ __forceinline__ void ldw(const uint8_t * p, uint32_t (&v)[8]) {
+    if constexpr (ALIGN == 16) {
+#pragma unroll
+        for (int i = 0; i < NW / 4; ++i) {
+            const uint4 a = __ldg((const uint4 *) p + i);
+            v[4 * i] = a.x; v[4 * i + 1] = a.y; v[4 * i + 2] = a.z; v[4 * i + 3] = a.w;
+        }
+    } else if constexpr (ALIGN == 4) {
+#pragma unroll
+        for (int i = 0; i < NW; ++i) v[i] = ld32(p + 4 * i);
+    } else {
+#pragma unroll
+        for (int i = 0; i < NW; ++i) v[i] = ld32_2(p + 4 * i);
+    }
+}
+
+// the four bits (x >> 4i) & 15 of x spread to bit 0 of four bytes
+__device__ __forceinline__ uint32_t spread4(uint32_t x, int i) {
+    const uint32_t b = (x >> (4 * i)) & 15u;
+    return (b & 1u) | ((b & 2u) << 7) | ((b & 4u) << 14) | ((b & 8u) << 21);
+}
+
+// 12 scale bytes of a Q4_K / Q5_K block -> the 6-bit scale and min of sub-block j (k_scale_min)
+__device__ __forceinline__ void scale_min_k(uint32_t s0, uint32_t s1, uint32_t s2, int j, int & sc, int & mn) {
+    auto byte = [&](int x) -> int {
+        const uint32_t w = x < 4 ? s0 : x < 8 ? s1 : s2;
+        return (int) ((w >> (8 * (x & 3))) & 255u);
+    };
+    if (j < 4) {
+        sc = byte(j) & 63;
+        mn = byte(j + 4) & 63;
+    } else {
+        sc = (byte(j + 4) & 15) | ((byte(j - 4) >> 6) << 4);
+        mn = (byte(j + 4) >> 4) | ((byte(j) >> 6) << 4);
+    }
+}
 
 template <int TYPE>
 __device__ __forceinline__ void decode_chunk(const uint8_t * __restrict__ row, int c, Chunk & k) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) k.q[i] = 0;
     k.sc0 = k.sc1 = 1;
     k.mn0 = k.mn1 = 0;
     k.dm = 0.0f;
     if constexpr (TYPE == T_Q4_0 || TYPE == T_Q4_1) {
-        const uint8_t * b = row + (size_t) c * (TYPE == T_Q4_0 ? 18 : 20);
-        const uint8_t * qs = b + (TYPE == T_Q4_0 ? 2 : 4);
-        k.d = ld_h2f(b);
-        if constexpr (TYPE == T_Q4_1) k.dm = ld_h2f(b + 2);
-        const int off = TYPE == T_Q4_0 ? 8 : 0;
+        constexpr bool M1 = TYPE == T_Q4_1;
+        const uint8_t * b = row + (size_t) c * (M1 ? 20 : 18);
+        uint32_t v[8];
+        if constexpr (M1) {
+            const uint32_t dm = ld32(b);
+            k.d = h2f(dm);
+            k.dm = h2f(dm >> 16);
+            ldw<4, 4>(b + 4, v);
+        } else {
+            k.d = h2f(ld16(b));
+            ldw<2, 4>(b + 2, v);
+        }
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const int byte = __ldg(qs + j);
-            put(k.q, j, (byte & 15) - off);
-            put(k.q, j + 16, (byte >> 4) - off);
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t lo = v[i] & 0x0f0f0f0fu, hi = (v[i] >> 4) & 0x0f0f0f0fu;
+            k.q[i] = M1 ? lo : __vsub4(lo, 0x08080808u);
+            k.q[i + 4] = M1 ? hi : __vsub4(hi, 0x08080808u);
         }
     } else if constexpr (TYPE == T_Q5_0 || TYPE == T_Q5_1) {
-        const uint8_t * b = row + (size_t) c * (TYPE == T_Q5_0 ? 22 : 24);
-        const int ho = TYPE == T_Q5_0 ? 2 : 4;
-        const uint8_t * qs = b + ho + 4;
-        k.d = ld_h2f(b);
-        if constexpr (TYPE == T_Q5_1) k.dm = ld_h2f(b + 2);
-        const uint32_t qh = (uint32_t) b[ho] | ((uint32_t) b[ho + 1] << 8) | ((uint32_t) b[ho + 2] << 16) |
-                            ((uint32_t) b[ho + 3] << 24);
-        const int off = TYPE == T_Q5_0 ? 16 : 0;
+        constexpr bool M1 = TYPE == T_Q5_1;
+        const uint8_t * b = row + (size_t) c * (M1 ? 24 : 22);
+        uint32_t v[8], qh;
+        if constexpr (M1) {
+            const uint32_t dm = ld32(b);
+            k.d = h2f(dm);
+            k.dm = h2f(dm >> 16);
+            qh = ld32(b + 4);
+            ldw<4, 4>(b + 8, v);
+        } else {
+            k.d = h2f(ld16(b));
+            qh = ld32_2(b + 2);
+            ldw<2, 4>(b + 6, v);
+        }
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            const int byte = __ldg(qs + j);
-            put(k.q, j, ((byte & 15) | (int) (((qh >> j) & 1u) << 4)) - off);
-            put(k.q, j + 16, ((byte >> 4) | (int) (((qh >> (j + 16)) & 1u) << 4)) - off);
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t lo = (v[i] & 0x0f0f0f0fu) | (spread4(qh, i) << 4);
+            const uint32_t hi = ((v[i] >> 4) & 0x0f0f0f0fu) | (spread4(qh, i + 4) << 4);
+            k.q[i] = M1 ? lo : __vsub4(lo, 0x10101010u);
+            k.q[i + 4] = M1 ? hi : __vsub4(hi, 0x10101010u);
         }
     } else if constexpr (TYPE == T_Q8_0) {
         const uint8_t * b = row + (size_t) c * 34;
-        k.d = ld_h2f(b);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            k.q[i] = (uint32_t) b[2 + 4 * i] | ((uint32_t) b[3 + 4 * i] << 8) | ((uint32_t) b[4 + 4 * i] << 16) |
-                     ((uint32_t) b[5 + 4 * i] << 24);
-        }
+        k.d = h2f(ld16(b));
+        ldw<2, 8>(b + 2, k.q);
     } else if constexpr (TYPE == T_Q4_K || TYPE == T_Q5_K) {
+        constexpr bool K5 = TYPE == T_Q5_K;
         const int j = c & 7;
-        const uint8_t * b = row + (size_t) (c >> 3) * (TYPE == T_Q4_K ? 144 : 176);
-        k.d = ld_h2f(b);
-        k.dm = ld_h2f(b + 2);
+        const uint8_t * b = row + (size_t) (c >> 3) * (K5 ? 176 : 144);
+        const uint32_t dm = ld32(b);
+        k.d = h2f(dm);
+        k.dm = h2f(dm >> 16);
         int sc, mn;
-        k_scale_min(b + 4, j, sc, mn);
+        scale_min_k(ld32(b + 4), ld32(b + 8), ld32(b + 12), j, sc, mn);
         k.sc0 = k.sc1 = sc;
         k.mn0 = k.mn1 = mn;
-        const uint8_t * qs = b + (TYPE == T_Q4_K ? 16 : 48) + 32 * (j >> 1);
+        uint32_t v[8];
+        ldw<16, 8>(b + (K5 ? 48 : 16) + 32 * (j >> 1), v);
         const int sh = 4 * (j & 1);
+        if constexpr (K5) {
+            uint32_t h[8];
+            ldw<16, 8>(b + 16, h);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-            int q = (__ldg(qs + e) >> sh) & 15;
-            if constexpr (TYPE == T_Q5_K) q |= ((__ldg(b + 16 + e) >> j) & 1) << 4;
-            put(k.q, e, q);
+            for (int i = 0; i < 8; ++i) k.q[i] = ((v[i] >> sh) & 0x0f0f0f0fu) | (((h[i] >> j) & 0x01010101u) << 4);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) k.q[i] = (v[i] >> sh) & 0x0f0f0f0fu;
         }
     } else if constexpr (TYPE == T_Q6_K) {
-        const int j = c & 7;
+        const int j = c & 7, h = j >> 2;
         const uint8_t * b = row + (size_t) (c >> 3) * 210;
-        const int h = j >> 2;
-        const uint8_t * ql = b + 64 * h + 32 * (j & 1);
-        const uint8_t * qh = b + 128 + 32 * h;
+        k.d = h2f(ld16(b + 208));
+        const uint32_t sc = ld16(b + 192 + 2 * j);
+        k.sc0 = (int) (int8_t) (sc & 255u);
+        k.sc1 = (int) (int8_t) (sc >> 8);
+        uint32_t lo[8], hi[8];
+        ldw<2, 8>(b + 64 * h + 32 * (j & 1), lo);
+        ldw<2, 8>(b + 128 + 32 * h, hi);
         const int lsh = 4 * ((j & 3) >> 1), hsh = 2 * (j & 3);
-        k.d = ld_h2f(b + 208);
-        k.sc0 = (int8_t) b[192 + 2 * j];
-        k.sc1 = (int8_t) b[193 + 2 * j];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-            const int lo = (__ldg(ql + e) >> lsh) & 15;
-            const int hi = (__ldg(qh + e) >> hsh) & 3;
-            put(k.q, e, (lo | (hi << 4)) - 32);
-        }
+        for (int i = 0; i < 8; ++i)
+            k.q[i] = __vsub4(((lo[i] >> lsh) & 0x0f0f0f0fu) | (((hi[i] >> hsh) & 0x03030303u) << 4), 0x20202020u);
     } else if constexpr (TYPE == T_Q2_K) {
         const int j = c & 7;
         const uint8_t * b = row + (size_t) (c >> 3) * 84;
-        k.d = ld_h2f(b + 80);
-        k.dm = ld_h2f(b + 82);
-        k.sc0 = b[2 * j] & 15;
-        k.mn0 = b[2 * j] >> 4;
-        k.sc1 = b[2 * j + 1] & 15;
-        k.mn1 = b[2 * j + 1] >> 4;
-        const uint8_t * qs = b + 16 + 32 * (j >> 2);
+        const uint32_t dm = ld32(b + 80);
+        k.d = h2f(dm);
+        k.dm = h2f(dm >> 16);
+        const uint32_t sc = ld16(b + 2 * j);
+        k.sc0 = (int) (sc & 15u);
+        k.mn0 = (int) ((sc >> 4) & 15u);
+        k.sc1 = (int) ((sc >> 8) & 15u);
+        k.mn1 = (int) (sc >> 12);
+        uint32_t v[8];
+        ldw<4, 8>(b + 16 + 32 * (j >> 2), v);
         const int sh = 2 * (j & 3);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) put(k.q, e, (__ldg(qs + e) >> sh) & 3);
+        for (int i = 0; i < 8; ++i) k.q[i] = (v[i] >> sh) & 0x03030303u;
     } else if constexpr (TYPE == T_Q3_K) {
         const int j = c & 7;
         const uint8_t * b = row + (size_t) (c >> 3) * 110;
-        const uint8_t * sc = b + 96;
-        k.d = ld_h2f(b + 108);
+        k.d = h2f(ld16(b + 108));
+        const uint32_t s01 = ld32_2(b + 96), s23 = ld32_2(b + 100), s45 = ld32_2(b + 104);
+        auto byte = [&](int x) -> int {
+            const uint32_t w = x < 4 ? s01 : x < 8 ? s23 : s45;
+            return (int) ((w >> (8 * (x & 3))) & 255u);
+        };
         auto scale = [&](int s) {
-            const int lo = (sc[s & 7] >> (4 * (s >> 3))) & 15;
-            const int hi = (sc[8 + (s & 3)] >> (2 * (s >> 2))) & 3;
+            const int lo = (byte(s & 7) >> (4 * (s >> 3))) & 15;
+            const int hi = (byte(8 + (s & 3)) >> (2 * (s >> 2))) & 3;
             return (lo | (hi << 4)) - 32;
         };
         k.sc0 = scale(2 * j);
         k.sc1 = scale(2 * j + 1);
-        const uint8_t * qs = b + 32 + 32 * (j >> 2);
+        uint32_t qs[8], hm[8];
+        ldw<2, 8>(b + 32 + 32 * (j >> 2), qs);
+        ldw<2, 8>(b, hm);
         const int sh = 2 * (j & 3);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-            const int ql = (__ldg(qs + e) >> sh) & 3;
-            const int hb = (__ldg(b + e) >> j) & 1;
-            put(k.q, e, ql - ((hb ^ 1) << 2));
-        }
+        for (int i = 0; i < 8; ++i)
+            k.q[i] = __vsub4(((qs[i] >> sh) & 0x03030303u) | (((hm[i] >> j) & 0x01010101u) << 2), 0x04040404u);
     }
 }
 
@@ -324,37 +387,52 @@ __device__ __forceinline__ void decode_floats(const uint8_t * __restrict__ row, 
     }
 }
 
-constexpr int MP = 8;       // activation rows per warp
+constexpr int MP = 8;       // activation rows per pass
 
-// out[m][n] = W[n] . x[m] (+ bias[n]); one warp per weight row n and 8 rows m
+// rows of W per warp: quantized weights share each activation load across 4 rows; float
+// weights (the classifier, usually a handful of rows) take one
+template <int TYPE> __host__ __device__ constexpr int rows_per_warp() { return vec_dot_family(TYPE) <= FAM_BF16 ? 1 : 4; }
+
+// out[m][n] = W[n] . x[m] (+ bias[n]).  A warp takes R consecutive weight rows and 8 activation
+// rows; lane L takes the 32-weight chunks L, L + 32, ... of those rows.  Each chunk of each row is
+// decoded once (wide loads) and each 32-code activation chunk is loaded once for the R rows.  A
+// chunk's dot products are exact integers (dp4a); its fp32 term (d_x * d * isum - d_x * dmin * msum
+// for the K-quants, d_w * d_x * isum (+ m_w * s_x) for the legacy types) goes into the lane's sum,
+// and the 32 lanes' sums are added at the end.  ggml's own SIMD kernels likewise turn per-lane
+// integer sums into fp32 before adding them; only the order of the fp32 additions differs.
 template <int TYPE>
 __global__ void __launch_bounds__(256) mul_mat_kernel(const uint8_t * __restrict__ w, size_t row_bytes, int N, int K,
                                                       const uint8_t * __restrict__ act, size_t stride, int M,
                                                       const float * __restrict__ bias, float * __restrict__ out) {
     constexpr int FAM = vec_dot_family(TYPE);
+    constexpr int R = rows_per_warp<TYPE>();
     const int lane = threadIdx.x & 31;
-    const int n = (int) (blockIdx.y * (blockDim.x >> 5) + (threadIdx.x >> 5));
+    const int n0 = (int) ((blockIdx.y * (blockDim.x >> 5) + (threadIdx.x >> 5)) * R);
+    if (n0 >= N) return;                                   // warp-uniform
     const int m0 = blockIdx.x * MP;
-    if (n >= N) return;
     const int mcount = min(MP, M - m0);
-    const uint8_t * wr = w + (size_t) n * row_bytes;
     const int n_chunks = K / 32;
-    float acc[MP];
+    // rows past N / M repeat the last one (computed, not stored), so every pass runs the same code
+    const uint8_t * wr[R];
 #pragma unroll
-    for (int i = 0; i < MP; ++i) acc[i] = 0.0f;
+    for (int r = 0; r < R; ++r) wr[r] = w + (size_t) min(n0 + r, N - 1) * row_bytes;
+    const uint8_t * ar[MP];
+#pragma unroll
+    for (int i = 0; i < MP; ++i) ar[i] = act + (size_t) min(m0 + i, M - 1) * stride;
+    float acc[R][MP];
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int i = 0; i < MP; ++i) acc[r][i] = 0.0f;
 
-    for (int c0 = 0; c0 < n_chunks; c0 += 32) {
-        const int c = c0 + lane;
-        const bool valid = c < n_chunks;
+    for (int c = lane; c < n_chunks; c += 32) {
         if constexpr (FAM == FAM_F32 || FAM == FAM_F16 || FAM == FAM_BF16) {
-            if (!valid) continue;
             float wv[32];
-            decode_floats<TYPE>(wr, c, wv);
+            decode_floats<TYPE>(wr[0], c, wv);
 #pragma unroll
             for (int i = 0; i < MP; ++i) {
-                if (i >= mcount) break;
-                const float4 * xp = (const float4 *) (act + (size_t) (m0 + i) * stride) + 8 * c;
-                float s = acc[i];
+                const float4 * xp = (const float4 *) ar[i] + 8 * c;
+                float s = acc[0][i];
 #pragma unroll
                 for (int v4 = 0; v4 < 8; ++v4) {
                     const float4 a = __ldg(xp + v4);
@@ -363,62 +441,61 @@ __global__ void __launch_bounds__(256) mul_mat_kernel(const uint8_t * __restrict
                     s = __fmaf_rn(wv[4 * v4 + 2], a.z, s);
                     s = __fmaf_rn(wv[4 * v4 + 3], a.w, s);
                 }
-                acc[i] = s;
+                acc[0][i] = s;
             }
         } else {
-            Chunk k;
-            if (valid) decode_chunk<TYPE>(wr, c, k);
+            Chunk k[R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) decode_chunk<TYPE>(wr[r], c, k[r]);
 #pragma unroll
             for (int i = 0; i < MP; ++i) {
-                if (i >= mcount) break;         // warp-uniform
-                const uint8_t * ar = act + (size_t) (m0 + i) * stride;
-                int s0 = 0, s1 = 0;
-                if (valid) {
-                    const uint4 a = __ldg((const uint4 *) (ar + 32 * (size_t) c));
-                    const uint4 b = __ldg((const uint4 *) (ar + 32 * (size_t) c + 16));
-                    s0 = __dp4a((int) k.q[0], (int) a.x, s0);
-                    s0 = __dp4a((int) k.q[1], (int) a.y, s0);
-                    s0 = __dp4a((int) k.q[2], (int) a.z, s0);
-                    s0 = __dp4a((int) k.q[3], (int) a.w, s0);
-                    s1 = __dp4a((int) k.q[4], (int) b.x, s1);
-                    s1 = __dp4a((int) k.q[5], (int) b.y, s1);
-                    s1 = __dp4a((int) k.q[6], (int) b.z, s1);
-                    s1 = __dp4a((int) k.q[7], (int) b.w, s1);
-                }
-                if constexpr (FAM == FAM_Q8_0 || FAM == FAM_Q8_1) {
-                    if (valid) {
-                        const float * dx = (const float *) (ar + K);
-                        acc[i] = __fadd_rn(acc[i], __fmul_rn(__fmul_rn(k.d, dx[c]), (float) (s0 + s1)));
-                        if constexpr (FAM == FAM_Q8_1) acc[i] = __fadd_rn(acc[i], __fmul_rn(k.dm, dx[K / 32 + c]));
-                    }
+                const uint4 a = __ldg((const uint4 *) (ar[i] + 32 * (size_t) c));
+                const uint4 b = __ldg((const uint4 *) (ar[i] + 32 * (size_t) c) + 1);
+                float dx, sx = 0.0f;
+                int b0 = 0, b1 = 0;
+                if constexpr (FAM == FAM_Q8_K) {
+                    dx = __ldg((const float *) (ar[i] + K) + (c >> 3));
+                    // bsum sits at K + 4 * (K / 256): 4-byte aligned only
+                    const int32_t * bs = (const int32_t *) (ar[i] + K + 4 * (size_t) (K / 256)) + 2 * c;
+                    b0 = __ldg(bs);
+                    b1 = __ldg(bs + 1);
                 } else {
-                    int ip = 0, mp = 0;
-                    if (valid) {
-                        const int32_t * bs = (const int32_t *) (ar + K + 4 * (size_t) (K / 256));
-                        ip = k.sc0 * s0 + k.sc1 * s1;
-                        mp = k.mn0 * bs[2 * c] + k.mn1 * bs[2 * c + 1];
-                    }
-                    // the 8 lanes of one 256-weight block: exact integer sums
+                    dx = __ldg((const float *) (ar[i] + K) + c);
+                    if constexpr (FAM == FAM_Q8_1) sx = __ldg((const float *) (ar[i] + K) + K / 32 + c);
+                }
 #pragma unroll
-                    for (int o = 1; o < 8; o <<= 1) {
-                        ip += __shfl_xor_sync(0xffffffffu, ip, o);
-                        mp += __shfl_xor_sync(0xffffffffu, mp, o);
-                    }
-                    if (valid && (lane & 7) == 0) {
-                        const float dx = ((const float *) (ar + K))[c >> 3];
-                        acc[i] = __fadd_rn(acc[i], __fmul_rn(__fmul_rn(dx, k.d), (float) ip));
-                        acc[i] = __fsub_rn(acc[i], __fmul_rn(__fmul_rn(dx, k.dm), (float) mp));
+                for (int r = 0; r < R; ++r) {
+                    int s0 = __dp4a((int) k[r].q[0], (int) a.x, 0);
+                    s0 = __dp4a((int) k[r].q[1], (int) a.y, s0);
+                    s0 = __dp4a((int) k[r].q[2], (int) a.z, s0);
+                    s0 = __dp4a((int) k[r].q[3], (int) a.w, s0);
+                    int s1 = __dp4a((int) k[r].q[4], (int) b.x, 0);
+                    s1 = __dp4a((int) k[r].q[5], (int) b.y, s1);
+                    s1 = __dp4a((int) k[r].q[6], (int) b.z, s1);
+                    s1 = __dp4a((int) k[r].q[7], (int) b.w, s1);
+                    if constexpr (FAM == FAM_Q8_K) {
+                        const int ip = k[r].sc0 * s0 + k[r].sc1 * s1;
+                        const int mp = k[r].mn0 * b0 + k[r].mn1 * b1;
+                        acc[r][i] = __fmaf_rn(__fmul_rn(dx, k[r].d), (float) ip, acc[r][i]);
+                        acc[r][i] = __fmaf_rn(-__fmul_rn(dx, k[r].dm), (float) mp, acc[r][i]);
+                    } else {
+                        acc[r][i] = __fmaf_rn(__fmul_rn(k[r].d, dx), (float) (s0 + s1), acc[r][i]);
+                        if constexpr (FAM == FAM_Q8_1) acc[r][i] = __fmaf_rn(k[r].dm, sx, acc[r][i]);
                     }
                 }
             }
         }
     }
 #pragma unroll
-    for (int i = 0; i < MP; ++i) {
-        float s = acc[i];
+    for (int r = 0; r < R; ++r) {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
-        if (lane == 0 && i < mcount) out[(size_t) (m0 + i) * N + n] = bias ? __fadd_rn(s, bias[n]) : s;
+        for (int i = 0; i < MP; ++i) {
+            float s = acc[r][i];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+            const int n = n0 + r;
+            if (lane == 0 && i < mcount && n < N) out[(size_t) (m0 + i) * N + n] = bias ? __fadd_rn(s, bias[n]) : s;
+        }
     }
 }
 
@@ -479,7 +556,8 @@ template <int TYPE>
 void launch_mul_mat(const void * w, int N, int K, const uint8_t * act, size_t stride, int M, const float * bias,
                     float * out, cudaStream_t st) {
     const size_t row_bytes = (size_t) K / blck_size(TYPE) * type_size(TYPE);
-    const dim3 grid((unsigned) ((M + MP - 1) / MP), (unsigned) ((N + 7) / 8));
+    const int rows = 8 * rows_per_warp<TYPE>();                // weight rows per 256-thread block
+    const dim3 grid((unsigned) ((M + MP - 1) / MP), (unsigned) ((N + rows - 1) / rows));
     mul_mat_kernel<TYPE><<<grid, 256, 0, st>>>((const uint8_t *) w, row_bytes, N, K, act, stride, M, bias, out);
 }
 
@@ -500,6 +578,10 @@ int nxk_mul_mat(int type, const void * w, int N, int K, const float * x, int M, 
     if (fam == FAM_NONE || N <= 0 || K <= 0 || M < 0 || (K & 31) || !w || !out || (M > 0 && (!x || !workspace)))
         return NXK_EINVAL;
     if (fam == FAM_Q8_K && (K & 255)) return NXK_EINVAL;
+    // 16-byte loads of the weight rows, of x and of the converted rows
+    if (((uintptr_t) w & 15) || ((uintptr_t) x & 15) || ((uintptr_t) workspace & 15) || ((uintptr_t) out & 3) ||
+        ((uintptr_t) bias & 3))
+        return NXK_EINVAL;
     if (N > 65535 * 8) return NXK_EINVAL;
     if (M == 0) return NXK_OK;
     const cudaStream_t st = S(stream);
@@ -540,7 +622,8 @@ int nxk_gelu_norm(const float * x, const float * w, float eps, int T, int C, flo
 }
 
 int nxk_gather_rows(const float * x, int C, const int32_t * idx, int n, float * out, void * stream) {
-    if (n < 0 || C <= 0 || (C & 3) || !x || !idx || !out) return NXK_EINVAL;
+    if (n < 0 || C <= 0 || (C & 3) || !x || !idx || !out || ((uintptr_t) x & 15) || ((uintptr_t) out & 15))
+        return NXK_EINVAL;
     if (n == 0) return NXK_OK;
     const size_t total = (size_t) n * (C / 4);
     gather_rows_kernel<<<(unsigned) ((total + 255) / 256), 256, 0, S(stream)>>>(x, C, idx, n, out);

@@ -5,8 +5,8 @@ the CPU checkers.
 Bars:
 * the activation conversion of nxk_mul_mat (Q8_K / Q8_0 / Q8_1 codes and scales,
   F16 / BF16 rounding) is bit-identical to ggml's restated in oracle/vecdot.c;
-* nxk_mul_mat's outputs: the integer block dots are exact and only the fp32 sum
-  of the block terms runs in another order, so |got - want| <= 1e-5 * sum|w||x|;
+* nxk_mul_mat's outputs: the integer chunk dots are exact and only the fp32 sums
+  of the chunk terms run in another order, so |got - want| <= 1e-5 * sum|w||x|;
 * the head entry points against the reference's own (oracle/_ref, on the host
   CPU): the int8 path is bit-exact, GELU uses CUDA's erff where the reference
   uses the C library's (they may differ in the last place), and that can flip an
