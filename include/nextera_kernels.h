@@ -39,6 +39,10 @@ extern "C" {
 /* device-side error word of the current device: returns it and clears it
  * (synchronises the stream).  Nonzero = a kernel gave up on a bounded wait. */
 NEXTERA_API int32_t nxk_take_error(void * stream);
+/* Failure-path self-test: one thread waits up to limit_ns (<= 1 s) on an mbarrier that nothing
+ * completes, with the GEMM pipeline's bounded wait, then records a timeout (0x1ff) in the error
+ * word that nxk_take_error returns.  The context stays usable. */
+NEXTERA_API int nxk_selftest_wait(int64_t limit_ns, void * stream);
 
 /* ---- weights: build_i8_weight (:1010-1049), on the device ----
  * blocks: n_out rows of GGUF blocks of `type` (any of F32 F16 BF16 Q4_0 Q4_1

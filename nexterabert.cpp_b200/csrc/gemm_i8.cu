@@ -38,12 +38,13 @@
 
 namespace nxk {
 
-extern __device__ int g_error;
+// this file's device error word (a kernel that gave up on a bounded wait); nxk_take_error reads it
+// through gemm_take_error, since without relocatable device code every file has its own variables
+__device__ int g_gemm_error;
 
 namespace gemm {
 
 constexpr int BM = 128, BN = 128, BKB = 128;      // tile rows, tile cols, K bytes per stage
-constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BKB, B_BYTES = BN * BKB, STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 32 * (2 + EPI_WARPS);
@@ -52,13 +53,22 @@ constexpr int TMEM_COLS = ACC * BN;                 // all 512 columns
 constexpr int MAX_BLK = 12;                         // K <= 3072
 constexpr int SCALE_FLOATS = 2 * MAX_BLK * BN;           // one slot: sw [block][128 cols], sx [128 rows][block]
 constexpr int SCALE_BYTES = 2 * SCALE_FLOATS * 4;        // two slots
-constexpr int OUT_BYTES = EPI_WARPS * 32 * 64 * 4;       // each epilogue warp's 32 x 64 output slice (2 swizzled boxes)
 constexpr int AMX_BYTES = 2 * 4 * 2 * 32 * 4;              // quantizing epilogues: [unit parity][quad][half][lane] maxima
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + OUT_BYTES + SCALE_BYTES + AMX_BYTES + 1024 /* alignment */ +
-                           256 /* barriers */;
 constexpr uint32_t IDESC = idesc_i8(BM, BN);
 
-enum : int { ERR_PRODUCER = 0x101, ERR_MMA = 0x102, ERR_EPILOGUE = 0x103 };
+// Shared memory per epilogue.  The operand ring is what keeps the MMAs fed: the copies of a stage
+// take 1-2 us from L2 under load, so the bytes in flight set the supply rate.  The fp32 epilogue
+// stages its output one 32 x 32 box per warp at a time (4 KB), which leaves room for a fifth stage;
+// the quantizing epilogues park a whole 32 x 64 slice per warp (8 KB) and keep four.
+template <int EPI> struct Smem {
+    static constexpr int STAGES = EPI == 0 ? 5 : 4;
+    static constexpr int OUT_BYTES = EPI_WARPS * 32 * (EPI == 0 ? 32 : 64) * 4;
+    static constexpr int BYTES = STAGES * STAGE_BYTES + OUT_BYTES + SCALE_BYTES + AMX_BYTES + 1024 /* alignment */ +
+                                 256 /* barriers */;
+    static_assert(BYTES <= 232448, "shared memory per block");
+};
+
+enum : int { ERR_PRODUCER = 0x101, ERR_MMA = 0x102, ERR_EPILOGUE = 0x103, ERR_SELFTEST = 0x1ff };
 
 // Epilogues.  EPI_F32: fp32 output (TMA store, or TMA reduce-add into the residual).  The other two
 // finish the row op that the reference applies to the layer's output and quantize the result for the
@@ -112,11 +122,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
            const __grid_constant__ CUtensorMap tm_out, const Args a) {
     constexpr int SUB = EPI == EPI_F32 ? 1 : 2;                     // tiles per unit
+    constexpr int STAGES = Smem<EPI>::STAGES, OUT_BYTES = Smem<EPI>::OUT_BYTES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
     uint8_t * sA = smem;
     uint8_t * sB = smem + STAGES * A_BYTES;
-    float * so = (float *) (sB + STAGES * B_BYTES);                   // [EPI_WARPS][2][32 rows][32 floats], 1024-aligned
+    float * so = (float *) (sB + STAGES * B_BYTES);                   // per warp [32 rows][32 or 64 floats], 1024-aligned
     float * scl = (float *) ((uint8_t *) so + OUT_BYTES);             // [2][SCALE_FLOATS]
     float * amx = (float *) ((uint8_t *) scl + SCALE_BYTES);          // [2][4][2][32]
     uint64_t * bars = (uint64_t *) ((uint8_t *) amx + AMX_BYTES);
@@ -196,7 +207,7 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
             }
             if (!ok) {
                 *abort_flag = 1;
-                atomicExch(&g_error, ERR_PRODUCER);
+                atomicExch(&g_gemm_error, ERR_PRODUCER);
             }
             // every issued copy lands before the CTA may exit
             const uint32_t first = it > STAGES ? it - STAGES : 0;
@@ -236,7 +247,7 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
             }
             if (!ok) {
                 *abort_flag = 1;
-                atomicExch(&g_error, ERR_MMA);
+                atomicExch(&g_gemm_error, ERR_MMA);
             }
             // the last MMAs complete before TMEM is released
             if (kb > 0) mbar_wait(smem_u32(&accf[(kb - 1) % ACC]), ((kb - 1) / ACC) & 1);
@@ -377,38 +388,36 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
                 continue;
             }
             if (nc < a.N) {
-                // this warp's 32 x 64 slice -> shared memory (two 32 x 32 boxes in the 128-byte
-                // swizzle: 16-byte chunk c of row r at chunk c ^ (r % 8)) -> one TMA store or
-                // reduce-add per box; rows past T are clipped by the tensor map
-                float * sbox = so + (warp - 2) * 2048;
-                if (lane == 0) bulk_wait_read();               // the previous tile's boxes have been read
-                __syncwarp();
+                // this warp's 32 x 64 slice leaves as two 32 x 32 boxes, one after the other through
+                // the warp's 4 KB of shared memory (128-byte swizzle: 16-byte chunk c of row r at
+                // chunk c ^ (r % 8)), each by one TMA store or reduce-add; rows past T are clipped by
+                // the tensor map
+                float * sbox = so + (warp - 2) * 1024;
+                const int y = m0 + 32 * quad;
 #pragma unroll
                 for (int hb = 0; hb < 2; ++hb) {
-                    float * rowp = sbox + hb * 1024 + lane * 32;
+                    if (lane == 0) bulk_wait_read();           // the box before has been read
+                    __syncwarp();
+                    float * rowp = sbox + lane * 32;
 #pragma unroll
                     for (int c = 0; c < 8; ++c) {
                         const float2 lo = f[16 * hb + 2 * c], hi = f[16 * hb + 2 * c + 1];
                         *(float4 *) (rowp + 4 * (c ^ (lane & 7))) = make_float4(lo.x, lo.y, hi.x, hi.y);
                     }
-                }
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                    const int y = m0 + 32 * quad;
-#pragma unroll
-                    for (int hb = 0; hb < 2; ++hb) {
-                        if (a.accumulate) tma_reduce_add_2d(&tm_out, nc + 32 * hb, y, smem_u32(sbox + hb * 1024));
-                        else              tma_store_2d(&tm_out, nc + 32 * hb, y, smem_u32(sbox + hb * 1024));
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (a.accumulate) tma_reduce_add_2d(&tm_out, nc + 32 * hb, y, smem_u32(sbox));
+                        else              tma_store_2d(&tm_out, nc + 32 * hb, y, smem_u32(sbox));
+                        bulk_commit();
                     }
-                    bulk_commit();
                 }
             }
         }
         if (lane == 0) bulk_wait_all();
         if (!ok) {
             *abort_flag = 1;
-            atomicExch(&g_error, ERR_EPILOGUE);
+            atomicExch(&g_gemm_error, ERR_EPILOGUE);
         }
     }
 
@@ -491,14 +500,34 @@ template <int EPI>
 int launch(const CUtensorMap & ma, const CUtensorMap & mb, const CUtensorMap & mo, const Args & a, cudaStream_t s) {
     static std::once_flag attr_once;
     std::call_once(attr_once, []() {
-        cudaFuncSetAttribute(gemm_i8_tc<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        cudaFuncSetAttribute(gemm_i8_tc<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem<EPI>::BYTES);
     });
     const int grid = min(a.n_units, sm_count());
-    gemm_i8_tc<EPI><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, mo, a);
+    gemm_i8_tc<EPI><<<grid, THREADS, Smem<EPI>::BYTES, s>>>(ma, mb, mo, a);
     return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
 }
 
+// An mbarrier that nothing ever completes, waited on for limit_ns: the same bounded wait and error
+// report as the GEMM's pipeline uses, made to run out on purpose (the wait ends, nothing faults).
+__global__ void wait_selftest_kernel(uint64_t limit_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bar), 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && !mbar_wait_ns(smem_u32(&bar), 0, limit_ns)) atomicExch(&g_gemm_error, ERR_SELFTEST);
+}
+
 } // namespace gemm
+
+int gemm_take_error() {
+    int v = 0, zero = 0;
+    cudaMemcpyFromSymbol(&v, g_gemm_error, sizeof(int));
+    cudaMemcpyToSymbol(g_gemm_error, &zero, sizeof(int));
+    return v;
+}
+
 } // namespace nxk
 
 using namespace nxk;
@@ -585,6 +614,12 @@ int nxk_linear_i8_simt(const int8_t * xq, const float * sx, int T, const int8_t 
     if (!n) return NXK_OK;
     nxk::gemm::gemm_i8_simt<<<(unsigned) ((n + 255) / 256), 256, 0, (cudaStream_t) stream>>>(
         xq, sx, T, w8, sw, K, N, res, out, nullptr);
+    return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
+}
+
+int nxk_selftest_wait(int64_t limit_ns, void * stream) {
+    if (limit_ns <= 0 || limit_ns > 1000000000) return NXK_EINVAL;
+    nxk::gemm::wait_selftest_kernel<<<1, 32, 0, (cudaStream_t) stream>>>((uint64_t) limit_ns);
     return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
 }
 

@@ -52,15 +52,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Waits for the phase with the given parity to complete; false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+// Waits for the phase with the given parity to complete; false after limit_ns without it.
+__device__ __forceinline__ bool mbar_wait_ns(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (;;) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (globaltimer() - t0 > NXK_WAIT_NS) return false;
+        if (globaltimer() - t0 > limit_ns) return false;
     }
 }
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) { return mbar_wait_ns(bar, parity, NXK_WAIT_NS); }
 
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const void * tmap) {

@@ -21,6 +21,7 @@
 namespace nxk {
 
 __device__ int g_error;
+int gemm_take_error();      // gemm_i8.cu
 
 constexpr int ROW_THREADS = 256;     // 8 rows per block
 
@@ -620,7 +621,8 @@ int32_t nxk_take_error(void * stream) {
     cudaStreamSynchronize(S(stream));
     cudaMemcpyFromSymbol(&v, g_error, sizeof(int));
     cudaMemcpyToSymbol(g_error, &zero, sizeof(int));
-    return v;
+    const int g = gemm_take_error();        // the GEMM's own word (cleared as well)
+    return v ? v : g;
 }
 
 int nxk_quantize(const float * x, int T, int C, int8_t * q, float * sx, void * stream) {

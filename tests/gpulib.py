@@ -43,6 +43,7 @@ def load_lib(path=None):
     L = ctypes.CDLL(str(path))
     sig = {
         "nxk_take_error": ([vp], ctypes.c_int32),
+        "nxk_selftest_wait": ([ctypes.c_int64, vp], c_int),
         "nxk_expand_weight": ([c_int, vp, c_int, c_int, vp, vp, vp, vp], c_int),
         "nxk_embed": ([c_int, vp, c_int, c_int, vp, c_int, c_int, vp, c_int, vp, vp, vp], c_int),
         "nxk_linear_i8": ([vp, vp, c_int, vp, vp, c_int, c_int, vp, vp, vp], c_int),

@@ -342,3 +342,20 @@ def test_embed_bit_exact(ops, oracle):
     assert rc == 0
     assert ops.L.nxk_take_error(None) != 0
     assert np.all(host(out)[5] == 0)
+
+
+def test_bounded_wait_reports_timeout(ops, oracle):
+    """A pipeline wait that runs out ends the kernel with an error word, not a hang; the context
+    stays usable (the GEMM after it is still bit-exact)."""
+    L = ops.L
+    assert L.nxk_take_error(None) == 0
+    assert L.nxk_selftest_wait(0, None) != 0                     # limits outside (0, 1 s] are refused
+    assert L.nxk_selftest_wait(20_000_000, None) == 0            # 20 ms on an mbarrier nothing completes
+    assert L.nxk_take_error(None) == 0x1FF
+    assert L.nxk_take_error(None) == 0                           # reading clears it
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((300, 1024)).astype(np.float32)
+    w = (0.02 * rng.standard_normal((512, 1024))).astype(np.float32)
+    w8, sw, _ = oracle.build_i8_weight(int(QT.Q8_0), sm.quantize_rows(w, QT.Q8_0), 1024, 512)
+    xq, xs = oracle.quantize_rows(x)
+    assert np.array_equal(ops.linear(xq, xs, w8, sw), oracle.linear_i8(xq, xs, w8, sw))
