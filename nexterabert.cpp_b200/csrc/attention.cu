@@ -28,6 +28,7 @@
 // tiles.  The softmax max must be known before any exp, so the pass over the
 // keys runs three times: max, then exp-sum, then the weighted sum of values
 // (scores are recomputed each time; O(T) memory for any document length).
+#include "attention_plan.hpp"
 #include "common.cuh"
 #include "nextera_kernels.h"
 
@@ -41,12 +42,6 @@ namespace attn {
 constexpr int D = 64;
 constexpr int QT = 32;      // queries per tile
 constexpr int KT = 32;      // keys per shared-memory tile
-
-struct Item {
-    int q0, q1;      // query rows [q0, q1), all in one document
-    int k0, k1;      // keys the tile may touch
-    int doc;
-};
 
 // exp for the softmax tail: correctly rounded fp32 exp (see above)
 __device__ __forceinline__ float exp_tail(float x) { return (float) exp((double) x); }
@@ -264,7 +259,6 @@ attn_kernel(const float * __restrict__ q, const float * __restrict__ k, const fl
 //           the keys in order; the tile's weights are staged in shared memory,
 //           zero outside a query's range (fma(0, v, o) leaves o unchanged).
 // ---------------------------------------------------------------------------
-constexpr int QT3 = 64;            // queries per work unit
 
 // 16-byte asynchronous global -> shared copies (both addresses 16-byte aligned)
 __device__ __forceinline__ void cp_async16(void * dst, const void * src) {
@@ -650,12 +644,6 @@ size_t n_items(const int32_t * len, int n_docs, int qt) {
 constexpr int SLOTS_PER_SM = 4;
 constexpr size_t SCRATCH_BUDGET = (size_t) 24 << 30;
 
-struct Scratch {
-    int slot_keys = 0;
-    int slots = 0;
-    size_t bytes = 0;
-};
-
 Scratch scratch_plan(const int32_t * len, int n_docs, int half) {
     int max_len = 0;
     for (int d = 0; d < n_docs; ++d) max_len = std::max(max_len, (int) len[d]);
@@ -670,6 +658,40 @@ Scratch scratch_plan(const int32_t * len, int n_docs, int half) {
     sp.slots = (int) slots;
     sp.bytes = slots * slot_bytes;
     return sp;
+}
+
+int launch_planned(const float * q, const float * k, const float * v, int T, int Tk, int koff, int H, int G,
+                   int half, const float * scale, const int32_t * doc_start, const int32_t * doc_len,
+                   const Item * d_items, size_t n_items_, const Scratch & sp, float * scratch, float * out,
+                   cudaStream_t s) {
+    const int rep = H / G;
+    if (rep != 1 && rep != 2 && rep != 4) return NXK_EINVAL;     // 128 * rep threads per block
+    if (n_items_ == 0) return NXK_OK;
+    const Item * it = d_items;
+    const long long n_units = (long long) n_items_ * G;
+    if (n_units > INT32_MAX) return NXK_EINVAL;
+    // persistent grid: no more CTAs than can be resident at once (each owns a scratch slot)
+    int dev = 0, sms = 148, per_sm = 1;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    auto launch = [&](auto kernel, int rep_) {
+        const int threads = 128 * rep_;
+        const size_t smem_bytes = sizeof(float) * (size_t) (rep_ == 1 ? tiled_smem_floats<1>()
+                                                            : rep_ == 2 ? tiled_smem_floats<2>()
+                                                                        : tiled_smem_floats<4>());
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem_bytes);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem_bytes);
+        const long long resident = (long long) std::max(per_sm, 1) * std::max(sms, 1);
+        const unsigned grid = (unsigned) std::min<long long>(std::min<long long>(n_units, sp.slots), resident);
+        kernel<<<grid, threads, smem_bytes, s>>>(q, k, v, out, it, (int) n_units, G, scale, doc_start, doc_len, T, Tk,
+                                                 koff, H, half, scratch, sp.slot_keys);
+    };
+    switch (rep) {
+        case 1: launch(attn_tiled_kernel<1>, 1); break;
+        case 2: launch(attn_tiled_kernel<2>, 2); break;
+        default: launch(attn_tiled_kernel<4>, 4); break;
+    }
+    return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
 }
 
 } // namespace attn
@@ -718,32 +740,9 @@ int nxk_attention_kv(const float * q, const float * k, const float * v, int T, i
         cudaSuccess) {
         return NXK_ELAUNCH;
     }
-    const attn::Item * it = (const attn::Item *) workspace;
-    float * scratch = (float *) ((char *) workspace + item_bytes);
-    const long long n_units = (long long) items.size() * G;
-    if (n_units > INT32_MAX) return NXK_EINVAL;
-    // persistent grid: no more CTAs than can be resident at once (each owns a scratch slot)
-    int dev = 0, sms = 148, per_sm = 1;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    auto launch = [&](auto kernel, int rep_) {
-        const int threads = 128 * rep_;
-        const size_t smem_bytes = sizeof(float) * (size_t) (rep_ == 1 ? attn::tiled_smem_floats<1>()
-                                                            : rep_ == 2 ? attn::tiled_smem_floats<2>()
-                                                                        : attn::tiled_smem_floats<4>());
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem_bytes);
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem_bytes);
-        const long long resident = (long long) std::max(per_sm, 1) * std::max(sms, 1);
-        const unsigned grid = (unsigned) std::min<long long>(std::min<long long>(n_units, sp.slots), resident);
-        kernel<<<grid, threads, smem_bytes, s>>>(q, k, v, out, it, (int) n_units, G, scale, doc_start, doc_len, T, Tk,
-                                                 koff, H, half, scratch, sp.slot_keys);
-    };
-    switch (rep) {
-        case 1: launch(attn::attn_tiled_kernel<1>, 1); break;
-        case 2: launch(attn::attn_tiled_kernel<2>, 2); break;
-        default: launch(attn::attn_tiled_kernel<4>, 4); break;
-    }
-    return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
+    return attn::launch_planned(q, k, v, T, Tk, koff, H, G, half, scale, doc_start, doc_len,
+                                (const attn::Item *) workspace, items.size(), sp,
+                                (float *) ((char *) workspace + item_bytes), out, s);
 }
 
 } // extern "C"

@@ -18,6 +18,7 @@
 #include "nextera_kernels.h"
 #include "gguf.hpp"
 #include "nccl_dl.hpp"
+#include "attention_plan.hpp"
 
 #include <cuda_runtime.h>
 
@@ -142,6 +143,25 @@ struct nextera_context {
     profiler prof;
     double last_ms = 0.0;
     int64_t launches = 0;          // kernels launched since load (all calls)
+    size_t stage_need = 0;         // pinned staging bytes of the last batch laid out
+
+    // Forwards of a batch shape seen before replay as a CUDA graph (host calls, up to GRAPH_MAX_T
+    // tokens): the shape's metadata sits in its own pinned staging buffer, the graph's first node
+    // uploads it (with the call's token ids written in first) and its last ones copy the results to
+    // pinned buffers.  An entry is dropped when a device buffer it uses has been reallocated.
+    struct GraphEntry {
+        std::vector<int32_t> key;          // lengths, then a flags word
+        cudaGraphExec_t exec = nullptr;
+        void * stage = nullptr;
+        float * h_pooled = nullptr, * h_hidden = nullptr;
+        size_t o_tok = 0, o_typ = 0;
+        std::vector<const void *> sig;     // the device buffers baked into the graph
+        int64_t launches = 0;
+        uint64_t used = 0;
+    };
+    std::vector<GraphEntry> graphs;
+    std::vector<std::vector<int32_t>> seen;   // recent shapes (a graph is made on the second one)
+    uint64_t graph_clock = 0;
 
     bool has(const std::string & n) const {
         return i8.count(n) || f32.count(n) || taps.count(n) || raw.count(n) ||
@@ -530,6 +550,12 @@ void nextera_free(struct nextera_context * c) {
     if (!c) return;
     cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
+    for (auto & g : c->graphs) {
+        if (g.exec) cudaGraphExecDestroy(g.exec);
+        if (g.stage) cudaFreeHost(g.stage);
+        if (g.h_pooled) cudaFreeHost(g.h_pooled);
+        if (g.h_hidden) cudaFreeHost(g.h_hidden);
+    }
     for (auto & m : c->prof.marks) cudaEventDestroy(m.first);
     if (c->h_stage) cudaFreeHost(c->h_stage);
     if (c->shard_comm) nxs::nccl().comm_destroy(c->shard_comm);
@@ -788,9 +814,14 @@ bool ensure_arena(nextera_context & c, const Batch & b) {
               c.Q1.reserve((size_t) T * std::max(I, C)) && c.Q1s.reserve(sizeof(float) * T * nb_W) &&
               c.Q2.reserve((size_t) T * C) && c.Q2s.reserve(sizeof(float) * T * nb_C);
     // staged metadata: row_doc T, brow_doc nb, start / len / bstart / blen per document, tokens T,
-    // types T (each padded to 64 entries), then one SSMax scale per (attention layer, document)
-    const size_t meta = sizeof(int32_t) * ((size_t) 3 * T + (size_t) b.nb + 4 * (size_t) b.n_docs + 8 * 64) +
+    // types T (each padded to 64 entries), one SSMax scale per (attention layer, document), then the
+    // attention plans (token rows banded and full, HRA block rows; 5 ints per item)
+    const size_t plan_ints = 5 * (2 * nxk::attn::n_items(b.len.data(), b.n_docs, nxk::attn::QT3) +
+                                  nxk::attn::n_items(b.blen.data(), b.n_docs, nxk::attn::QT3)) + 3 * 64;
+    const size_t meta = sizeof(int32_t) * ((size_t) 3 * T + (size_t) b.nb + 4 * (size_t) b.n_docs + 9 * 64 +
+                                           plan_ints) +
                         sizeof(float) * (size_t) b.n_docs * (size_t) std::max(hp.n_layer, 1) + 256;
+    c.stage_need = meta;
     ok = ok && c.meta.reserve(meta);
     size_t ws = std::max(nxk_attention_workspace(b.len.data(), b.n_docs, -1),
                          nxk_attention_workspace(b.blen.data(), b.n_docs, -1));
@@ -840,7 +871,8 @@ bool halo_rows(const ShardRun & sh, float * x, int rows, int width, int h, cudaS
 
 int run_encoder(nextera_context & c, const Batch & b, float rope0_base, const int32_t * tokens,
                 const int32_t * types, bool on_host, cudaStream_t s, float * d_hidden_out, float * d_pooled_out,
-                int normalize, float ** hidden_dev, const ShardRun * sh = nullptr) {
+                int normalize, float ** hidden_dev, const ShardRun * sh = nullptr, void * stage = nullptr,
+                size_t * tok_off = nullptr, size_t * typ_off = nullptr) {
     const hparams & hp = c.hp;
     const int T = b.T, C = hp.n_embd, H = hp.n_head, G = hp.n_kv_head, D = hp.head_dim;
     if (!ensure_arena(c, b) || !ensure_rope(c, 0, b.max_len, rope0_base) ||
@@ -849,7 +881,7 @@ int run_encoder(nextera_context & c, const Batch & b, float rope0_base, const in
         return 2;
     }
     // stage the layout (and host tokens) in pinned memory, one copy to the device
-    int32_t * hs = (int32_t *) c.h_stage;
+    int32_t * hs = (int32_t *) (stage ? stage : c.h_stage);
     int32_t * dm = c.meta.as<int32_t>();
     size_t o = 0;
     auto put = [&](const int32_t * src, size_t n) {
@@ -868,6 +900,8 @@ int run_encoder(nextera_context & c, const Batch & b, float rope0_base, const in
         o_tok = put(tokens, T);
         if (use_types) o_typ = put(types, T);
     }
+    if (tok_off) *tok_off = o_tok;
+    if (typ_off) *typ_off = o_typ;
     // SSMax scales per attention layer and document (host math as in the reference)
     std::vector<int> scale_off(hp.n_layer, -1);
     float * hsc = (float *) (hs + o);
@@ -885,7 +919,34 @@ int run_encoder(nextera_context & c, const Batch & b, float rope0_base, const in
             hsc[n_sc++] = base_scale * (swa ? 1.0f : fw.ssmax_scale(pre, n));
         }
     }
-    const size_t stage_ints = o + n_sc;
+    // the attention plans of this batch (one per kind of rows and band the layers use), staged with
+    // the rest so one copy uploads everything; sharded runs plan per call instead (nxk_attention_kv)
+    struct APlan {
+        bool blocks;
+        int half;
+        size_t n, off;
+        nxk::attn::Scratch sp;
+    };
+    std::vector<APlan> aplans;
+    size_t o_end = o + (n_sc + 63) / 64 * 64;
+    if (!sh) {
+        std::vector<nxk::attn::Item> items;
+        for (int l = 0; l < n_layer; ++l) {
+            const mixer_type mt = hp.block_types[l];
+            if (mt == MIX_LILY) continue;
+            const bool blocks = mt == MIX_HRA;
+            const int half = mt == MIX_SWA ? std::max(1, hp.swa_window / 2) : -1;
+            bool have = false;
+            for (const APlan & p : aplans) have = have || (p.blocks == blocks && p.half == half);
+            if (have) continue;
+            const std::vector<int32_t> & st = blocks ? b.bstart : b.start, & ln = blocks ? b.blen : b.len;
+            nxk::attn::plan(st.data(), ln.data(), b.n_docs, half, nxk::attn::QT3, blocks ? b.nb : T, items);
+            aplans.push_back({blocks, half, items.size(), o_end, nxk::attn::scratch_plan(ln.data(), b.n_docs, half)});
+            memcpy(hs + o_end, items.data(), items.size() * sizeof(nxk::attn::Item));
+            o_end += (items.size() * sizeof(nxk::attn::Item) / sizeof(int32_t) + 63) / 64 * 64;
+        }
+    }
+    const size_t stage_ints = sh ? o + n_sc : o_end;
     cudaMemcpyAsync(dm, hs, stage_ints * sizeof(int32_t), cudaMemcpyHostToDevice, s);
     const float * d_scales = (const float *) (dm + o);
     Layout L;
@@ -967,8 +1028,22 @@ int run_encoder(nextera_context & c, const Batch & b, float rope0_base, const in
             }
             if (!ok) fw.ok = false;
         }
-        fw.rows(nxk_attention_kv(q, k, v, rows, Tk, koff, H, G, D, half, scale, start, len, b.n_docs, h_start.data(),
-                                 h_len.data(), c.attn_ws.p, c.attn_ws.bytes, y, s), "attention");
+        if (sh) {
+            fw.rows(nxk_attention_kv(q, k, v, rows, Tk, koff, H, G, D, half, scale, start, len, b.n_docs,
+                                     h_start.data(), h_len.data(), c.attn_ws.p, c.attn_ws.bytes, y, s), "attention");
+            return;
+        }
+        const bool blocks = &h_start == &b.bstart;
+        const APlan * ap = nullptr;
+        for (const APlan & p : aplans) if (p.blocks == blocks && p.half == half) ap = &p;
+        if (!ap || ap->sp.bytes > c.attn_ws.bytes) {
+            fprintf(stderr, "nexterabert: no attention plan for this layer\n");
+            fw.ok = false;
+            return;
+        }
+        fw.rows(nxk::attn::launch_planned(q, k, v, rows, Tk, koff, H, G, half, scale, start, len,
+                                     (const nxk::attn::Item *) (dm + ap->off), ap->n, ap->sp, (float *) c.attn_ws.p, y, s),
+                "attention");
     };
 
     // halo rows of a token convolution's input (sharded runs only); returns the halo to read
@@ -1107,6 +1182,79 @@ void collect_profile(nextera_context & c) {
     pr.marks.clear();
 }
 
+constexpr int GRAPH_MAX_T = 32768;       // larger batches keep the GPU busy without graphs
+constexpr size_t GRAPH_CACHE = 8;
+
+std::vector<const void *> graph_sig(const nextera_context & c) {
+    return { c.X.p, c.X2.p, c.U.p, c.Fa.p, c.Fb.p, c.Fc.p, c.Q1.p, c.Q1s.p, c.Q2.p, c.Q2s.p, c.meta.p,
+             c.attn_ws.p, c.pooled.p, c.rope_cos[0].p, c.rope_cos[1].p, c.rope_sin[0].p, c.rope_sin[1].p };
+}
+
+void drop_graph(nextera_context::GraphEntry & g) {
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+    if (g.stage) cudaFreeHost(g.stage);
+    if (g.h_pooled) cudaFreeHost(g.h_pooled);
+    if (g.h_hidden) cudaFreeHost(g.h_hidden);
+    g = nextera_context::GraphEntry();
+}
+
+// Records the forward of batch b as a graph (the same shape has run eagerly before, so the arena,
+// rope tables and pinned staging already fit it and nothing below allocates device memory).
+// Returns the new entry, or nullptr (and the call runs eagerly) if capture fails.
+nextera_context::GraphEntry * capture_graph(nextera_context * c, const Batch & b, float rope0,
+                                            const int32_t * tokens, const int32_t * types, bool want_hidden,
+                                            int32_t normalize, std::vector<int32_t> key) {
+    const int C = c->hp.n_embd;
+    // the same sizing calls run_encoder makes, outside the capture (no-ops when they already fit)
+    if (!ensure_arena(*c, b) || !ensure_rope(*c, 0, b.max_len, rope0) ||
+        !ensure_rope(*c, 1, b.max_len, c->hp.swa_rope_base))
+        return nullptr;
+    nextera_context::GraphEntry g;
+    g.key = std::move(key);
+    if (cudaMallocHost(&g.stage, c->stage_need) != cudaSuccess ||
+        cudaMallocHost((void **) &g.h_pooled, sizeof(float) * (size_t) b.n_docs * C) != cudaSuccess ||
+        (want_hidden && cudaMallocHost((void **) &g.h_hidden, sizeof(float) * (size_t) b.T * C) != cudaSuccess)) {
+        cudaGetLastError();
+        drop_graph(g);
+        return nullptr;
+    }
+    const int64_t l0 = c->launches;
+    if (cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaGetLastError();
+        drop_graph(g);
+        return nullptr;
+    }
+    float * hid = nullptr;
+    int rc = run_encoder(*c, b, rope0, tokens, types, true, c->stream, nullptr, nullptr, normalize, &hid, nullptr,
+                         g.stage, &g.o_tok, &g.o_typ);
+    if (rc == 0) {
+        cudaMemcpyAsync(g.h_pooled, c->pooled.p, sizeof(float) * (size_t) b.n_docs * C, cudaMemcpyDeviceToHost,
+                        c->stream);
+        if (want_hidden)
+            cudaMemcpyAsync(g.h_hidden, hid, sizeof(float) * (size_t) b.T * C, cudaMemcpyDeviceToHost, c->stream);
+    }
+    cudaGraph_t graph = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(c->stream, &graph);
+    if (rc != 0 || e != cudaSuccess || !graph || cudaGraphInstantiate(&g.exec, graph, 0) != cudaSuccess) {
+        cudaGetLastError();
+        if (graph) cudaGraphDestroy(graph);
+        drop_graph(g);
+        return nullptr;
+    }
+    cudaGraphDestroy(graph);
+    g.launches = c->launches - l0;
+    g.sig = graph_sig(*c);
+    if (c->graphs.size() >= GRAPH_CACHE) {
+        size_t old = 0;
+        for (size_t i = 1; i < c->graphs.size(); ++i)
+            if (c->graphs[i].used < c->graphs[old].used) old = i;
+        drop_graph(c->graphs[old]);
+        c->graphs.erase(c->graphs.begin() + (ptrdiff_t) old);
+    }
+    c->graphs.push_back(std::move(g));
+    return &c->graphs.back();
+}
+
 int32_t encode_host(nextera_context * c, const int32_t * tokens, const int32_t * types, const int32_t * lengths,
                     int32_t n_seqs, float * hidden, float * pooled, int32_t normalize) {
     const auto t0 = std::chrono::steady_clock::now();
@@ -1116,6 +1264,45 @@ int32_t encode_host(nextera_context * c, const int32_t * tokens, const int32_t *
     if (!tokens) return 1;
     int rc = prepare(*c, tokens, types, lengths, n_seqs, true, b, rope0);
     if (rc) return rc;
+    const bool use_types = types && c->hp.n_types > 0;
+    if (!c->prof.enabled && b.T <= GRAPH_MAX_T) {
+        std::vector<int32_t> key(b.len);
+        key.push_back((use_types ? 1 : 0) | (hidden ? 2 : 0) | (normalize ? 4 : 0) | ((c->debug_n_layers + 1) << 3));
+        nextera_context::GraphEntry * g = nullptr;
+        for (auto & e : c->graphs) if (e.key == key) g = &e;
+        if (g && g->sig != graph_sig(*c)) {
+            drop_graph(*g);
+            c->graphs.erase(c->graphs.begin() + (g - c->graphs.data()));
+            g = nullptr;
+        }
+        if (!g && std::find(c->seen.begin(), c->seen.end(), key) != c->seen.end())
+            g = capture_graph(c, b, rope0, tokens, types, hidden != nullptr, normalize, key);
+        if (g) {
+            const int C = c->hp.n_embd;
+            g->used = ++c->graph_clock;
+            memcpy((int32_t *) g->stage + g->o_tok, tokens, sizeof(int32_t) * (size_t) b.T);
+            if (use_types) memcpy((int32_t *) g->stage + g->o_typ, types, sizeof(int32_t) * (size_t) b.T);
+            rc = 0;
+            if (cudaGraphLaunch(g->exec, c->stream) != cudaSuccess || cudaStreamSynchronize(c->stream) != cudaSuccess) {
+                fprintf(stderr, "nexterabert: device error: %s\n", cudaGetErrorString(cudaGetLastError()));
+                rc = 3;
+            } else if (int32_t e = nxk_take_error(c->stream)) {
+                fprintf(stderr, "nexterabert: a kernel timed out waiting on its pipeline (code 0x%x)\n", e);
+                rc = 3;
+            }
+            c->launches += g->launches;
+            if (rc == 0) {
+                if (pooled) memcpy(pooled, g->h_pooled, sizeof(float) * (size_t) n_seqs * C);
+                if (hidden) memcpy(hidden, g->h_hidden, sizeof(float) * (size_t) b.T * C);
+            }
+            c->last_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+            return rc;
+        }
+        if (std::find(c->seen.begin(), c->seen.end(), key) == c->seen.end()) {
+            if (c->seen.size() >= 32) c->seen.erase(c->seen.begin());
+            c->seen.push_back(std::move(key));
+        }
+    }
     float * hid = nullptr;
     rc = run_encoder(*c, b, rope0, tokens, types, true, c->stream, nullptr, nullptr, normalize, &hid);
     if (rc == 0) {

@@ -181,3 +181,35 @@ def test_cfg3_full_model_q4km(lib, oracle):
     print(f"cfg3: hidden rel err {rel:.2e}, min token cosine {cos:.8f}")
     m.close()
     o.close()
+
+
+def test_repeated_shapes_replay_graphs_bit_exact(lib, oracle):
+    """A batch shape seen before runs as a recorded CUDA graph: new token ids, the same bits as the
+    eager forward, whatever ran in between (other shapes, hidden on / off, segments)."""
+    hp = sm.tiny_hparams(n_types=2)
+    path = sm.cached_model("tiny_seg", hp, "Q4_K_M", seed=3)
+    m = Model(lib, path)
+    fresh = Model(lib, path)                    # a second context that never repeats a shape
+    shapes = [np.array([5, 17, 40], np.int32), np.array([64, 1, 130], np.int32)]
+    for it in range(4):
+        for si, lens in enumerate(shapes):
+            rng = np.random.default_rng(100 * it + si)
+            tok = rng.integers(0, 1000, int(lens.sum())).astype(np.int32)
+            types = rng.integers(0, 2, int(lens.sum())).astype(np.int32) if si == 1 else None
+            want_hidden = it != 2
+            rc, hid, pooled = m.encode(tok, lens, types=types, hidden=want_hidden)
+            assert rc == 0
+            # the reference result of this call: a context seeing the shape for the first time
+            fresh.close()
+            fresh = Model(lib, path)
+            rc2, hid2, pooled2 = fresh.encode(tok, lens, types=types, hidden=True)
+            assert rc2 == 0
+            assert np.array_equal(pooled, pooled2), (it, si)
+            if want_hidden:
+                assert np.array_equal(hid, hid2), (it, si)
+    # graphs were used: later calls of a shape launch the recorded kernels (same launch count)
+    n0 = lib.nextera_debug_launches(m.h)
+    rc, _, _ = m.encode(np.zeros(int(shapes[0].sum()), np.int32), shapes[0])
+    assert rc == 0 and lib.nextera_debug_launches(m.h) > n0
+    m.close()
+    fresh.close()
