@@ -9,22 +9,24 @@
 // the fp32 epilogue performs the same operations in the same order (ascending
 // B from 0, residual added last), so outputs are bit-identical.
 //
-// Kernel shape (one CTA per SM, persistent over 128x128 output tiles, tile
+// Kernel shape (one CTA per SM, persistent over 128 x 256 output tiles, tile
 // index n-fastest so the CTAs in flight share their activation tiles in L2):
-//   warp 0      TMA producer: 128x128-byte tiles of xq and w8 (SWIZZLE_128B)
-//               into a 4-stage shared-memory ring, and per tile the scales the
-//               epilogue needs (sw of its 128 columns, sx of its 128 rows) by
-//               bulk copy into a 2-slot ring, so the epilogue never waits on a
-//               global load
-//   warp 1      allocates TMEM (2 x 128 columns) and issues tcgen05.mma from one
-//               thread: 4 MMAs (K = 32 each) per 128-byte stage, one TMEM
+//   warp 0      TMA producer: 128-byte K slices of 128 rows of xq and 256 rows of
+//               w8 (SWIZZLE_128B) into a 3-stage shared-memory ring, and per tile
+//               the scales the epilogue needs (sw of its 256 columns, sx of its
+//               128 rows) by bulk copy into a 2-slot ring, so the epilogue never
+//               waits on a global load
+//   warp 1      allocates TMEM (2 x 256 columns) and issues tcgen05.mma (M 128,
+//               N 256) from one thread: 4 MMAs (K = 32 each) per stage, one TMEM
 //               accumulator per 256-input block, alternating between the two
 //   warps 2-9   epilogue: tcgen05.ld the block's int32 sums (warp w reads TMEM
-//               lane quadrant w % 4, half the columns), release the buffer,
-//               fold the block into fp32 registers; after the last block add the
-//               residual and store
+//               lane quadrant w % 4 and 128 of the columns), release the
+//               accumulator, fold the block into fp32 registers; after the last
+//               block finish the row op (if any) and store
 // The per-block accumulator switch is what lets the int32 sums be scaled per
-// block: the MMA of block B+1 runs while the epilogue drains block B.
+// block: the MMA of block B+1 runs while the epilogue drains block B.  A 256-wide
+// tile needs half the TMA loads per multiply-add of a 128-wide one and a quarter
+// fewer operand bytes: the copies, not the tensor pipe, set this kernel's rate.
 #include "common.cuh"
 #include "ptx.cuh"
 #include "nextera_kernels.h"
@@ -33,6 +35,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <cstdio>
 #include <cstring>
 #include <mutex>
 
@@ -44,25 +47,24 @@ __device__ int g_gemm_error;
 
 namespace gemm {
 
-constexpr int BM = 128, BN = 128, BKB = 128;      // tile rows, tile cols, K bytes per stage
+constexpr int BM = 128, BN = 256, BKB = 128;      // tile rows, tile cols, K bytes per stage
 constexpr int A_BYTES = BM * BKB, B_BYTES = BN * BKB, STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 32 * (2 + EPI_WARPS);
-constexpr int ACC = 4;                              // TMEM accumulators (one per 256-input block in flight)
+constexpr int ACC = 2;                              // TMEM accumulators (one per 256-input block in flight)
 constexpr int TMEM_COLS = ACC * BN;                 // all 512 columns
 constexpr int MAX_BLK = 12;                         // K <= 3072
-constexpr int SCALE_FLOATS = 2 * MAX_BLK * BN;           // one slot: sw [block][128 cols], sx [128 rows][block]
+constexpr int SCALE_FLOATS = MAX_BLK * BN + BM * MAX_BLK;  // one slot: sw [block][256 cols], sx [128 rows][block]
 constexpr int SCALE_BYTES = 2 * SCALE_FLOATS * 4;        // two slots
 constexpr int AMX_BYTES = 2 * 4 * 2 * 32 * 4;              // quantizing epilogues: [unit parity][quad][half][lane] maxima
 constexpr uint32_t IDESC = idesc_i8(BM, BN);
 
-// Shared memory per epilogue.  The operand ring is what keeps the MMAs fed: the copies of a stage
-// take 1-2 us from L2 under load, so the bytes in flight set the supply rate.  The fp32 epilogue
-// stages its output one 32 x 32 box per warp at a time (4 KB), which leaves room for a fifth stage;
-// the quantizing epilogues park a whole 32 x 64 slice per warp (8 KB) and keep four.
+// Shared memory per epilogue: a 3-stage ring of 48 KB operand stages (A 128 x 128 bytes, B 256 x 128
+// bytes), the scales of two tiles, and for the fp32 epilogue one 32 x 32 output box per warp (4 KB),
+// its 32 x 128 slice leaving one box at a time.
 template <int EPI> struct Smem {
-    static constexpr int STAGES = EPI == 0 ? 5 : 4;
-    static constexpr int OUT_BYTES = EPI_WARPS * 32 * (EPI == 0 ? 32 : 64) * 4;
+    static constexpr int STAGES = 3;
+    static constexpr int OUT_BYTES = EPI == 0 ? EPI_WARPS * 32 * 32 * 4 : 0;
     static constexpr int BYTES = STAGES * STAGE_BYTES + OUT_BYTES + SCALE_BYTES + AMX_BYTES + 1024 /* alignment */ +
                                  256 /* barriers */;
     static_assert(BYTES <= 232448, "shared memory per block");
@@ -87,7 +89,7 @@ struct Args {
     float * out;
     int T, N, K, n_blk, n_chunks, tiles_n, n_tiles;
     int accumulate;          // 1: out += result (the residual is `out` itself), by TMA reduce-add
-    int n_units;             // tiles (EPI_F32) or pairs of tiles (quantizing epilogues) to process
+    int n_units;             // tiles to process
     const float * z;         // EPI_GATE: the multiplier [T][N]
     int8_t * qout;           // quantizing epilogues: codes [T][N] (s8, the reference's u8 - 128)
     float * sqout;           // and scales [T][N / 256]
@@ -121,7 +123,6 @@ template <int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
            const __grid_constant__ CUtensorMap tm_out, const Args a) {
-    constexpr int SUB = EPI == EPI_F32 ? 1 : 2;                     // tiles per unit
     constexpr int STAGES = Smem<EPI>::STAGES, OUT_BYTES = Smem<EPI>::OUT_BYTES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
@@ -172,9 +173,7 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
         if (lane == 0) {
             uint32_t it = 0, tc = 0;
             bool ok = true;
-            for (int t_ = SUB * blockIdx.x, u_ = 0; ok && t_ < a.n_tiles;
-                 t_ += (++u_ % SUB) ? 1 : SUB * (gridDim.x - 1) + 1, ++tc) {
-                const int tile = t_;
+            for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x, ++tc) {
                 const int m0 = (tile / a.tiles_n) * BM, n0 = (tile % a.tiles_n) * BN;
                 {
                     // the tile's scales -> slot tc % 2: sw rows [block][n0, n0 + cols), sx rows [m0, m0 + rows)
@@ -220,8 +219,7 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
         if (lane == 0) {
             uint32_t it = 0, kb = 0;
             bool ok = true;
-            for (int t_ = SUB * blockIdx.x, u_ = 0; ok && t_ < a.n_tiles;
-                 t_ += (++u_ % SUB) ? 1 : SUB * (gridDim.x - 1) + 1) {
+            for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x) {
                 for (int b = 0; ok && b < a.n_blk; ++b, ++kb) {
                     const uint32_t acc = kb % ACC, use = kb / ACC;
                     if (use > 0 && !mbar_wait(smem_u32(&acce[acc]), (use - 1) & 1)) { ok = false; break; }
@@ -254,84 +252,76 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
         }
     } else {
         // ------------------------------------------------------------ epilogue
+        // warp w reads TMEM lane quadrant w % 4 (its 32 rows) and column half (w - 2) / 4 (128 columns)
         const int quad = warp & 3, halfc = (warp - 2) >> 2;
         const int row = 32 * quad + lane;
         uint32_t kb = 0, tc = 0, uc = 0;
         bool ok = true;
-        float am0 = 0.0f;                                              // quantizing: first tile's row maximum
-        for (int t_ = SUB * blockIdx.x, u_ = 0; ok && t_ < a.n_tiles;
-             t_ += (++u_ % SUB) ? 1 : SUB * (gridDim.x - 1) + 1, ++tc) {
-            const int tile = t_;
-            const int s2 = tile % SUB;                                 // which tile of the unit
+        for (int tile = blockIdx.x; ok && tile < a.n_tiles; tile += gridDim.x, ++tc) {
             const int m0 = (tile / a.tiles_n) * BM, n0 = (tile % a.tiles_n) * BN;
             const int t = m0 + row;
-            const int nc = n0 + 64 * halfc;
+            const int nc = n0 + 128 * halfc;
             const uint32_t sb = tc & 1;
             {
                 const bool got = mbar_wait(smem_u32(&sfull[sb]), (tc >> 1) & 1) && !*abort_flag;
                 if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
             }
-            const float * sws = scl + sb * SCALE_FLOATS + 64 * halfc;      // [block][128 cols], this warp's 64
+            const float * sws = scl + sb * SCALE_FLOATS + 128 * halfc;     // [block][256 cols], this warp's 128
             const float * sxs = scl + sb * SCALE_FLOATS + MAX_BLK * BN;    // [128 rows][block]
-            float2 f[32];
+            float2 f[64];
 #pragma unroll
-            for (int c = 0; c < 32; ++c) f[c] = make_float2(0.0f, 0.0f);
+            for (int c = 0; c < 64; ++c) f[c] = make_float2(0.0f, 0.0f);
             for (int b = 0; b < a.n_blk; ++b, ++kb) {
                 const uint32_t acc = kb % ACC, use = kb / ACC;
                 const bool got = mbar_wait(smem_u32(&accf[acc]), use & 1) && !*abort_flag;
                 if (!__all_sync(0xffffffffu, got)) { ok = false; break; }   // warp-uniform
                 tc_fence_after();
-                uint32_t r0[32], r1[32];
-                const uint32_t taddr = tmem + ((uint32_t) (32 * quad) << 16) + acc * BN + 64 * halfc;
-                tmem_ld_32x32b_x32(taddr, r0);
-                tmem_ld_32x32b_x32(taddr + 32, r1);
-                tmem_wait_ld();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(&acce[acc]));
-                if (nc >= a.N) continue;                                   // columns past N (N % 64 == 0)
+                const uint32_t taddr = tmem + ((uint32_t) (32 * quad) << 16) + acc * BN + 128 * halfc;
+                const bool live = nc < a.N;                                // columns past N (N % 64 == 0)
                 const float sxb = t < a.T ? sxs[row * a.n_blk + b] : 0.0f;
                 const float2 sx2 = make_float2(sxb, sxb);
                 const float2 nmagic = make_float2(-12582912.0f, -12582912.0f);   // x - m == x + (-m) exactly
                 const float4 * swp = (const float4 *) (sws + b * BN);
-                // f = fma(float(S) * sx, sw, f) per column, two columns per packed instruction;
-                // float(S) exact via the 1.5 * 2^23 bias (|S| <= 2^22)
+                // f = fma(float(S) * sx, sw, f) per column, two columns per packed instruction, 16 columns
+                // per TMEM load; float(S) exact via the 1.5 * 2^23 bias (|S| <= 2^22).  (Ten warps put
+                // three on one SM sub-partition, whose 16K registers then allow 168 per thread.)
 #pragma unroll
-                for (int c4 = 0; c4 < 8; ++c4) {
-                    const float4 w = swp[c4];
-                    const float2 s0 = __fadd2_rn(make_float2(__int_as_float((int) r0[4 * c4] + 0x4B400000),
-                                                             __int_as_float((int) r0[4 * c4 + 1] + 0x4B400000)), nmagic);
-                    const float2 s1 = __fadd2_rn(make_float2(__int_as_float((int) r0[4 * c4 + 2] + 0x4B400000),
-                                                             __int_as_float((int) r0[4 * c4 + 3] + 0x4B400000)), nmagic);
-                    f[2 * c4]     = __ffma2_rn(__fmul2_rn(s0, sx2), make_float2(w.x, w.y), f[2 * c4]);
-                    f[2 * c4 + 1] = __ffma2_rn(__fmul2_rn(s1, sx2), make_float2(w.z, w.w), f[2 * c4 + 1]);
-                }
+                for (int q8 = 0; q8 < 8; ++q8) {
+                    uint32_t r[16];
+                    tmem_ld_32x32b_x16(taddr + 16 * q8, r);
+                    tmem_wait_ld();
+                    if (!live) continue;
 #pragma unroll
-                for (int c4 = 0; c4 < 8; ++c4) {
-                    const float4 w = swp[8 + c4];
-                    const float2 s0 = __fadd2_rn(make_float2(__int_as_float((int) r1[4 * c4] + 0x4B400000),
-                                                             __int_as_float((int) r1[4 * c4 + 1] + 0x4B400000)), nmagic);
-                    const float2 s1 = __fadd2_rn(make_float2(__int_as_float((int) r1[4 * c4 + 2] + 0x4B400000),
-                                                             __int_as_float((int) r1[4 * c4 + 3] + 0x4B400000)), nmagic);
-                    f[16 + 2 * c4]     = __ffma2_rn(__fmul2_rn(s0, sx2), make_float2(w.x, w.y), f[16 + 2 * c4]);
-                    f[16 + 2 * c4 + 1] = __ffma2_rn(__fmul2_rn(s1, sx2), make_float2(w.z, w.w), f[16 + 2 * c4 + 1]);
+                    for (int c4 = 0; c4 < 4; ++c4) {
+                        const float4 w = swp[4 * q8 + c4];
+                        const float2 s0 = __fadd2_rn(make_float2(__int_as_float((int) r[4 * c4] + 0x4B400000),
+                                                                 __int_as_float((int) r[4 * c4 + 1] + 0x4B400000)), nmagic);
+                        const float2 s1 = __fadd2_rn(make_float2(__int_as_float((int) r[4 * c4 + 2] + 0x4B400000),
+                                                                 __int_as_float((int) r[4 * c4 + 3] + 0x4B400000)), nmagic);
+                        f[8 * q8 + 2 * c4]     = __ffma2_rn(__fmul2_rn(s0, sx2), make_float2(w.x, w.y), f[8 * q8 + 2 * c4]);
+                        f[8 * q8 + 2 * c4 + 1] = __ffma2_rn(__fmul2_rn(s1, sx2), make_float2(w.z, w.w), f[8 * q8 + 2 * c4 + 1]);
+                    }
                 }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&acce[acc]));
             }
             if (!ok) break;
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&sempty[sb]));             // scales slot free
             if (EPI != EPI_F32) {
-                // the row op on this tile's 64 columns of row t, then its maximum |v|
+                // the row op on this tile's 128 columns of row t, then the maximum |v| over the row's
+                // 256-column quantization block (this tile: the two warps of the quadrant hold its halves)
                 if (EPI == EPI_RELU2) {
 #pragma unroll
-                    for (int c = 0; c < 32; ++c) {
+                    for (int c = 0; c < 64; ++c) {
                         const float x0 = f[c].x > 0.0f ? f[c].x : 0.0f, x1 = f[c].y > 0.0f ? f[c].y : 0.0f;
                         f[c] = __fmul2_rn(make_float2(x0, x1), make_float2(x0, x1));
                     }
                 } else if (t < a.T) {
                     const float4 * zr = (const float4 *) (a.z + (size_t) t * a.N + nc);
 #pragma unroll
-                    for (int c4 = 0; c4 < 16; ++c4) {
+                    for (int c4 = 0; c4 < 32; ++c4) {
                         const float4 zz = zr[c4];
                         f[2 * c4] = __fmul2_rn(sigmoid8x2(f[2 * c4]), make_float2(zz.x, zz.y));
                         f[2 * c4 + 1] = __fmul2_rn(sigmoid8x2(f[2 * c4 + 1]), make_float2(zz.z, zz.w));
@@ -339,21 +329,10 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
                 }
                 float am = 0.0f;
 #pragma unroll
-                for (int c = 0; c < 32; ++c) am = fmaxf(am, fmaxf(fabsf(f[c].x), fabsf(f[c].y)));
-                float * rowp = so + (warp - 2) * 2048 + lane * 64;     // this warp's row, 16 swizzled chunks
-                if (s2 == 0) {
-                    // first tile of the unit: park the values until the second tile's are known
-#pragma unroll
-                    for (int c = 0; c < 16; ++c)
-                        *(float4 *) (rowp + 4 * (c ^ (lane & 7))) =
-                            make_float4(f[2 * c].x, f[2 * c].y, f[2 * c + 1].x, f[2 * c + 1].y);
-                    am0 = am;
-                    continue;
-                }
-                // second tile: the row's block maximum over both tiles and both column halves
+                for (int c = 0; c < 64; ++c) am = fmaxf(am, fmaxf(fabsf(f[c].x), fabsf(f[c].y)));
                 const uint32_t p = uc & 1;
                 float * ax = amx + ((p * 4 + quad) * 2) * 32;            // [half][lane]
-                ax[halfc * 32 + lane] = fmaxf(am0, am);
+                ax[halfc * 32 + lane] = am;
                 __syncwarp();
                 if (lane == 0) mbar_arrive(smem_u32(&xbar[quad]));
                 {
@@ -365,37 +344,30 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
                 if (t < a.T) {
                     const float inv = act_inv(amax);
                     const bool fast = isfinite(inv);
-                    const int n00 = n0 - BN;                                // the unit's first column
-                    uint4 * q0 = (uint4 *) (a.qout + (size_t) t * a.N + n00 + 64 * halfc);
-                    uint4 * q1 = (uint4 *) (a.qout + (size_t) t * a.N + n0 + 64 * halfc);
+                    uint4 * q = (uint4 *) (a.qout + (size_t) t * a.N + nc);
 #pragma unroll
-                    for (int c4 = 0; c4 < 4; ++c4) {
-                        const float4 v0 = *(const float4 *) (rowp + 4 * ((4 * c4 + 0) ^ (lane & 7)));
-                        const float4 v1 = *(const float4 *) (rowp + 4 * ((4 * c4 + 1) ^ (lane & 7)));
-                        const float4 v2 = *(const float4 *) (rowp + 4 * ((4 * c4 + 2) ^ (lane & 7)));
-                        const float4 v3 = *(const float4 *) (rowp + 4 * ((4 * c4 + 3) ^ (lane & 7)));
-                        q0[c4] = make_uint4(pack_codes(v0.x, v0.y, v0.z, v0.w, inv, fast), pack_codes(v1.x, v1.y, v1.z, v1.w, inv, fast),
-                                            pack_codes(v2.x, v2.y, v2.z, v2.w, inv, fast), pack_codes(v3.x, v3.y, v3.z, v3.w, inv, fast));
+                    for (int c4 = 0; c4 < 8; ++c4) {
                         const float2 * g = &f[8 * c4];
-                        q1[c4] = make_uint4(pack_codes(g[0].x, g[0].y, g[1].x, g[1].y, inv, fast),
-                                            pack_codes(g[2].x, g[2].y, g[3].x, g[3].y, inv, fast),
-                                            pack_codes(g[4].x, g[4].y, g[5].x, g[5].y, inv, fast),
-                                            pack_codes(g[6].x, g[6].y, g[7].x, g[7].y, inv, fast));
+                        q[c4] = make_uint4(pack_codes(g[0].x, g[0].y, g[1].x, g[1].y, inv, fast),
+                                           pack_codes(g[2].x, g[2].y, g[3].x, g[3].y, inv, fast),
+                                           pack_codes(g[4].x, g[4].y, g[5].x, g[5].y, inv, fast),
+                                           pack_codes(g[6].x, g[6].y, g[7].x, g[7].y, inv, fast));
                     }
-                    if (halfc == 0) a.sqout[(size_t) t * (a.N / 256) + n00 / 256] = act_scale(amax);
+                    if (halfc == 0) a.sqout[(size_t) t * (a.N / 256) + n0 / 256] = act_scale(amax);
                 }
                 __syncwarp();
                 continue;
             }
             if (nc < a.N) {
-                // this warp's 32 x 64 slice leaves as two 32 x 32 boxes, one after the other through
+                // this warp's 32 x 128 slice leaves as four 32 x 32 boxes, one after the other through
                 // the warp's 4 KB of shared memory (128-byte swizzle: 16-byte chunk c of row r at
                 // chunk c ^ (r % 8)), each by one TMA store or reduce-add; rows past T are clipped by
                 // the tensor map
                 float * sbox = so + (warp - 2) * 1024;
                 const int y = m0 + 32 * quad;
 #pragma unroll
-                for (int hb = 0; hb < 2; ++hb) {
+                for (int hb = 0; hb < 4; ++hb) {
+                    if (nc + 32 * hb >= a.N) break;                // warp-uniform
                     if (lane == 0) bulk_wait_read();           // the box before has been read
                     __syncwarp();
                     float * rowp = sbox + lane * 32;
@@ -476,13 +448,13 @@ bool make_out_map(CUtensorMap * m, const void * base, uint64_t rows, uint64_t N)
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// rows x K bytes, K-contiguous, boxes of 128 rows x 128 bytes in the 128-byte swizzle
-bool make_map(CUtensorMap * m, const void * base, uint64_t rows, uint64_t K) {
+// rows x K bytes, K-contiguous, boxes of box_rows rows x 128 bytes in the 128-byte swizzle
+bool make_map(CUtensorMap * m, const void * base, uint64_t rows, uint64_t K, int box_rows) {
     auto fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = { (cuuint64_t) K, (cuuint64_t) rows };
     cuuint64_t strides[1] = { (cuuint64_t) K };
-    cuuint32_t box[2] = { (cuuint32_t) BKB, (cuuint32_t) BM };
+    cuuint32_t box[2] = { (cuuint32_t) BKB, (cuuint32_t) box_rows };
     cuuint32_t estr[2] = { 1, 1 };
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -504,7 +476,9 @@ int launch(const CUtensorMap & ma, const CUtensorMap & mb, const CUtensorMap & m
     });
     const int grid = min(a.n_units, sm_count());
     gemm_i8_tc<EPI><<<grid, THREADS, Smem<EPI>::BYTES, s>>>(ma, mb, mo, a);
-    return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
+    const cudaError_t e = cudaPeekAtLastError();
+    if (e != cudaSuccess) fprintf(stderr, "nexterabert: int8 GEMM launch failed: %s\n", cudaGetErrorString(e));
+    return e == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
 }
 
 // An mbarrier that nothing ever completes, waited on for limit_ns: the same bounded wait and error
@@ -546,8 +520,9 @@ int nxk_linear_i8(const int8_t * xq, const float * sx, int T, const int8_t * w8,
     if (res && ((uintptr_t) res & 15)) return NXK_EINVAL;
     if (T == 0) return NXK_OK;
     CUtensorMap ma, mb, mo;
-    if (!make_map(&ma, xq, (uint64_t) T, (uint64_t) K) || !make_map(&mb, w8, (uint64_t) N, (uint64_t) K) ||
+    if (!make_map(&ma, xq, (uint64_t) T, (uint64_t) K, BM) || !make_map(&mb, w8, (uint64_t) N, (uint64_t) K, BN) ||
         !make_out_map(&mo, out, (uint64_t) T, (uint64_t) N)) {
+        fprintf(stderr, "nexterabert: int8 GEMM tensor map rejected (T %d, K %d, N %d)\n", T, K, N);
         return NXK_ELAUNCH;
     }
     // a residual other than `out` itself is copied into `out` first: the kernel accumulates in place
@@ -582,8 +557,10 @@ static int linear_q(int op, const int8_t * xq, const float * sx, int T, const in
     if (T == 0) return NXK_OK;
     CUtensorMap ma, mb, mo;
     memset(&mo, 0, sizeof(mo));                       // no fp32 output: the map is never used
-    if (!make_map(&ma, xq, (uint64_t) T, (uint64_t) K) || !make_map(&mb, w8, (uint64_t) N, (uint64_t) K))
+    if (!make_map(&ma, xq, (uint64_t) T, (uint64_t) K, BM) || !make_map(&mb, w8, (uint64_t) N, (uint64_t) K, BN)) {
+        fprintf(stderr, "nexterabert: int8 GEMM tensor map rejected (T %d, K %d, N %d)\n", T, K, N);
         return NXK_ELAUNCH;
+    }
     Args a;
     a.sx = sx; a.sw = sw; a.res = nullptr; a.out = nullptr;
     a.accumulate = 0;
@@ -592,7 +569,7 @@ static int linear_q(int op, const int8_t * xq, const float * sx, int T, const in
     a.n_chunks = (K + BKB - 1) / BKB;
     a.tiles_n = N / BN;
     a.n_tiles = ((T + BM - 1) / BM) * a.tiles_n;
-    a.n_units = a.n_tiles / 2;
+    a.n_units = a.n_tiles;
     a.z = z; a.qout = q; a.sqout = sq;
     return op == EPI_RELU2 ? launch<EPI_RELU2>(ma, mb, mo, a, stream) : launch<EPI_GATE>(ma, mb, mo, a, stream);
 }
