@@ -317,12 +317,96 @@ __global__ void __launch_bounds__(256) conv_kernel(const float * __restrict__ x,
     }
 }
 
+// Narrow rows (C = 32, 64 or 128: the Lily low-rank conv): a row is C / 8 lanes, so a warp takes
+// 256 / C rows at a time and a block 8 * 256 / C * NARROW_STEPS rows; otherwise as conv_kernel
+// (dwconv only), with the row's quantization block (all C columns) reduced over its lanes.
+constexpr int NARROW_STEPS = 4;
+
+template <int C>
+__global__ void __launch_bounds__(256) conv_narrow_kernel(const float * __restrict__ x, const float * __restrict__ r,
+                                                          const float * __restrict__ taps, int k, int halo,
+                                                          const int32_t * __restrict__ row_doc,
+                                                          const int32_t * __restrict__ doc_start,
+                                                          const int32_t * __restrict__ doc_len, int T,
+                                                          float * __restrict__ out, int8_t * __restrict__ q,
+                                                          float * __restrict__ sx) {
+    constexpr int LPR = C / 8;                       // lanes per row
+    constexpr int RPW = 32 / LPR;                    // rows per warp step
+    constexpr int ROWS = 8 * RPW * NARROW_STEPS;     // rows per block
+    extern __shared__ float4 conv_sm[];
+    float * P = (float *) conv_sm;                   // [ROWS + k - 1][C]
+    float * W = P + (size_t) (ROWS + k - 1) * C;     // [k][C]
+    const int t0 = blockIdx.x * ROWS, hk = k / 2;
+    const int n4 = (ROWS + k - 1) * (C / 4);
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+        const int rr = i / (C / 4), c4 = i % (C / 4);
+        const int tr = t0 - hk + rr;
+        if (tr >= -halo && tr < T + halo) ((float4 *) P)[i] = *(const float4 *) (x + (ptrdiff_t) tr * C + 4 * c4);
+    }
+    for (int i = threadIdx.x; i < k * (C / 4); i += blockDim.x) ((float4 *) W)[i] = ((const float4 *) taps)[i];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int sub = lane / LPR, c0 = 8 * (lane % LPR);
+    for (int step = 0; step < NARROW_STEPS; ++step) {
+        const int rr = (step * 8 + warp) * RPW + sub;
+        const int t = t0 + rr;
+        const bool on = t < T;                                       // whole lane groups
+        float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (on) {
+            const int d = row_doc[t];
+            const int lo = doc_start[d], hi = lo + doc_len[d];
+            const int j0 = max(0, lo - (t - hk)), j1 = min(k, hi - (t - hk));
+            if (r) ld8(r + (size_t) t * C + c0, v);
+            for (int j = j0; j < j1; ++j) {
+                float pv[8], wv[8];
+                ld8(P + (size_t) (rr + j) * C + c0, pv);
+                ld8(W + (size_t) j * C + c0, wv);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = __fmaf_rn(wv[e], pv[e], v[e]);
+            }
+        }
+        if (!q) {
+            if (on) {
+                float4 * o = (float4 *) (out + (size_t) t * C + c0);
+                o[0] = make_float4(v[0], v[1], v[2], v[3]);
+                o[1] = make_float4(v[4], v[5], v[6], v[7]);
+            }
+            continue;
+        }
+        // the row's maximum |v| over its LPR lanes (C <= 256: one quantization block)
+        float am = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) am = fmaxf(am, fabsf(v[e]));
+#pragma unroll
+        for (int o = 1; o < LPR; o <<= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+        if (on) {
+            const float inv = act_inv(am);
+            if (lane % LPR == 0) sx[t] = act_scale(am);
+            *(uint2 *) (q + (size_t) t * C + c0) =
+                make_uint2(pack4(v[0], v[1], v[2], v[3], inv), pack4(v[4], v[5], v[6], v[7], inv));
+        }
+    }
+}
+
 int launch_conv(bool lily, const float * x, const float * a, const float * r, const float * b, const float * taps,
                 int k, int halo, const int32_t * row_doc, const int32_t * doc_start, const int32_t * doc_len, int T,
                 int C, float * out, int8_t * q, float * sx, cudaStream_t s) {
     if (T < 0 || C <= 0 || (C & 31) || k <= 0 || k > CONV_KMAX || halo < 0 || (!q && !out) || (q && !sx))
         return NXK_EINVAL;
     if (T == 0) return NXK_OK;
+    if (!lily && (C == 32 || C == 64 || C == 128)) {
+        auto narrow = [&](auto kern, int c) {
+            const int rows = 8 * (256 / c) * NARROW_STEPS;
+            const size_t smem = sizeof(float) * (size_t) c * (size_t) (rows + 2 * k - 1);
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+            kern<<<(unsigned) ((T + rows - 1) / rows), 256, smem, s>>>(x, r, taps, k, halo, row_doc, doc_start,
+                                                                       doc_len, T, out, q, sx);
+        };
+        if (C == 32) narrow(conv_narrow_kernel<32>, 32);
+        else if (C == 64) narrow(conv_narrow_kernel<64>, 64);
+        else narrow(conv_narrow_kernel<128>, 128);
+        return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
+    }
     const dim3 grid((unsigned) ((T + CONV_ROWS - 1) / CONV_ROWS), (unsigned) ((C + 255) / 256));
     const size_t smem = conv_smem_bytes(k);
     auto go = [&](auto kern, const float * a_, const float * r_, const float * b_) {

@@ -157,7 +157,7 @@ def test_quantize_and_row_ops_bit_exact(ops, oracle, C):
     assert np.array_equal(q, wq) and np.array_equal(s, ws)
 
 
-@pytest.mark.parametrize("C,k", [(256, 5), (64, 5), (1024, 3)])
+@pytest.mark.parametrize("C,k", [(256, 5), (64, 5), (1024, 3), (32, 5), (128, 3), (64, 7)])
 def test_conv_ops_bit_exact(ops, oracle, C, k):
     from gpulib import P, dev
     L = cases.LENGTHS_SMALL
