@@ -621,19 +621,23 @@ __global__ void pool_finish_kernel(int n, int C, int normalize, float * __restri
 // ---------------------------------------------------------------------------
 constexpr int ERR_TOKEN_RANGE = 0x201;
 
-// one block per token row; threads stride over its C columns
-__global__ void __launch_bounds__(256) embed_kernel(int type, const uint8_t * __restrict__ table, size_t row_bytes,
+// One warp per token row: lane L decodes the 4 consecutive values 128 * i + 4L .. +3 (one 16-byte
+// store each), the block type fixed at compile time so the decoding of a block's header is shared
+// by the 4 values (each value is still the per-element formula of deq_elem).
+template <int TYPE>
+__global__ void __launch_bounds__(256) embed_kernel(const uint8_t * __restrict__ table, size_t row_bytes,
                                                     int n_rows, int C, const int32_t * __restrict__ tokens, int T,
                                                     int ttype, const uint8_t * __restrict__ ttable, size_t trow_bytes,
                                                     int tn_rows, const int32_t * __restrict__ types,
                                                     float * __restrict__ out) {
-    const int t = blockIdx.x;
+    const int t = (int) ((blockIdx.x * (size_t) blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
     if (t >= T) return;
     const int id = tokens[t];
     float * o = out + (size_t) t * C;
     if (id < 0 || id >= n_rows) {
-        for (int c = threadIdx.x; c < C; c += blockDim.x) o[c] = 0.0f;
-        if (threadIdx.x == 0) atomicExch(&g_error, ERR_TOKEN_RANGE);
+        for (int c = 4 * lane; c < C; c += 128) *(float4 *) (o + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (lane == 0) atomicExch(&g_error, ERR_TOKEN_RANGE);
         return;
     }
     const uint8_t * row = table + row_bytes * (size_t) id;
@@ -641,15 +645,20 @@ __global__ void __launch_bounds__(256) embed_kernel(int type, const uint8_t * __
     if (ttable) {
         ty = types[t];
         if (ty < 0 || ty >= tn_rows) {
-            if (threadIdx.x == 0) atomicExch(&g_error, ERR_TOKEN_RANGE);
+            if (lane == 0) atomicExch(&g_error, ERR_TOKEN_RANGE);
             ty = -1;
         }
     }
     const uint8_t * trow = ty >= 0 ? ttable + trow_bytes * (size_t) ty : nullptr;
-    for (int c = threadIdx.x; c < C; c += blockDim.x) {
-        float v = deq_elem(type, row, c);
-        if (trow) v = __fadd_rn(v, deq_elem(ttype, trow, c));
-        o[c] = v;
+    for (int c = 4 * lane; c < C; c += 128) {
+        float v[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = deq_elem(TYPE, row, c + e);
+        if (trow) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) v[e] = __fadd_rn(v[e], deq_elem(ttype, trow, c + e));
+        }
+        *(float4 *) (o + c) = make_float4(v[0], v[1], v[2], v[3]);
     }
 }
 
@@ -846,9 +855,28 @@ int nxk_embed(int type, const void * table, int n_rows, int C, const int32_t * t
     if (T == 0) return NXK_OK;
     const size_t rb = (size_t) (C / bs) * type_size(type);
     const size_t trb = ttable ? (size_t) (C / blck_size(ttype)) * type_size(ttype) : 0;
-    embed_kernel<<<(unsigned) T, 256, 0, S(stream)>>>(
-        type, (const uint8_t *) table, rb, n_rows, C, tokens, T, ttype, (const uint8_t *) ttable, trb, tn_rows, types,
-        out);
+    if (((uintptr_t) out & 15) || (C & 3)) return NXK_EINVAL;           // 16-byte stores
+    const unsigned grid = (unsigned) ((T + 7) / 8);
+    auto go = [&](auto kern) {
+        kern<<<grid, 256, 0, S(stream)>>>((const uint8_t *) table, rb, n_rows, C, tokens, T, ttype,
+                                          (const uint8_t *) ttable, trb, tn_rows, types, out);
+    };
+    switch (type) {
+        case T_F32: go(embed_kernel<T_F32>); break;
+        case T_F16: go(embed_kernel<T_F16>); break;
+        case T_BF16: go(embed_kernel<T_BF16>); break;
+        case T_Q4_0: go(embed_kernel<T_Q4_0>); break;
+        case T_Q4_1: go(embed_kernel<T_Q4_1>); break;
+        case T_Q5_0: go(embed_kernel<T_Q5_0>); break;
+        case T_Q5_1: go(embed_kernel<T_Q5_1>); break;
+        case T_Q8_0: go(embed_kernel<T_Q8_0>); break;
+        case T_Q2_K: go(embed_kernel<T_Q2_K>); break;
+        case T_Q3_K: go(embed_kernel<T_Q3_K>); break;
+        case T_Q4_K: go(embed_kernel<T_Q4_K>); break;
+        case T_Q5_K: go(embed_kernel<T_Q5_K>); break;
+        case T_Q6_K: go(embed_kernel<T_Q6_K>); break;
+        default: return NXK_EINVAL;
+    }
     return launched();
 }
 
