@@ -60,11 +60,12 @@ constexpr int AMX_BYTES = 2 * 4 * 2 * 32 * 4;              // quantizing epilogu
 constexpr uint32_t IDESC = idesc_i8(BM, BN);
 
 // Shared memory per epilogue: a 3-stage ring of 48 KB operand stages (A 128 x 128 bytes, B 256 x 128
-// bytes), the scales of two tiles, and for the fp32 epilogue one 32 x 32 output box per warp (4 KB),
-// its 32 x 128 slice leaving one box at a time.
+// bytes), the scales of two tiles, and one 4 KB output box per epilogue warp: for fp32 outputs a 32 x 32
+// box (the warp's 32 x 128 slice leaves one box at a time), for the quantizing epilogues the 32 rows x
+// 128 codes of its slice.
 template <int EPI> struct Smem {
     static constexpr int STAGES = 3;
-    static constexpr int OUT_BYTES = EPI == 0 ? EPI_WARPS * 32 * 32 * 4 : 0;
+    static constexpr int OUT_BYTES = EPI_WARPS * 4096;
     static constexpr int BYTES = STAGES * STAGE_BYTES + OUT_BYTES + SCALE_BYTES + AMX_BYTES + 1024 /* alignment */ +
                                  256 /* barriers */;
     static_assert(BYTES <= 232448, "shared memory per block");
@@ -96,18 +97,20 @@ struct Args {
 };
 
 // act_code of four values packed in a word.  `fast`: inv = 127 / amax is finite and |value| <= amax,
-// so |value * inv| <= 127.00002 and rounding to nearest is already the code (the reference's
-// saturation cannot trigger); a NaN product still gives the reference's -128.
-__device__ __forceinline__ uint32_t code_fast(float v) {
-    const int c = __float2int_rn(v);
-    return (uint32_t) (v == v ? c : -128) & 0xffu;
+// so |value * inv| <= 127.00002 and the reference's saturation cannot trigger: adding 1.5 * 2^23 then
+// rounds the product to the nearest integer, ties to even (the reference's rint), in the low mantissa
+// bits, whose low byte is the code; fmaxf turns a NaN product into -128, the reference's code for NaN.
+__device__ __forceinline__ uint32_t pack_fast(float a, float b, float c, float d, float inv) {
+    const float2 i2 = make_float2(inv, inv), m2 = make_float2(12582912.0f, 12582912.0f);
+    const float2 p = __fmul2_rn(make_float2(a, b), i2), q = __fmul2_rn(make_float2(c, d), i2);
+    const float2 pr = __fadd2_rn(make_float2(fmaxf(p.x, -128.0f), fmaxf(p.y, -128.0f)), m2);
+    const float2 qr = __fadd2_rn(make_float2(fmaxf(q.x, -128.0f), fmaxf(q.y, -128.0f)), m2);
+    const uint32_t lo = __byte_perm(__float_as_uint(pr.x), __float_as_uint(pr.y), 0x0040);
+    const uint32_t hi = __byte_perm(__float_as_uint(qr.x), __float_as_uint(qr.y), 0x0040);
+    return __byte_perm(lo, hi, 0x5410);
 }
 __device__ __forceinline__ uint32_t pack_codes(float a, float b, float c, float d, float inv, bool fast) {
-    if (fast) {
-        const float2 p = __fmul2_rn(make_float2(a, b), make_float2(inv, inv));
-        const float2 q = __fmul2_rn(make_float2(c, d), make_float2(inv, inv));
-        return code_fast(p.x) | (code_fast(p.y) << 8) | (code_fast(q.x) << 16) | (code_fast(q.y) << 24);
-    }
+    if (fast) return pack_fast(a, b, c, d, inv);
     return (uint32_t) (uint8_t) act_code(a, inv) | ((uint32_t) (uint8_t) act_code(b, inv) << 8) |
            ((uint32_t) (uint8_t) act_code(c, inv) << 16) | ((uint32_t) (uint8_t) act_code(d, inv) << 24);
 }
@@ -157,7 +160,7 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
         fence_barrier_init();
         tma_prefetch_desc(&tm_a);
         tma_prefetch_desc(&tm_b);
-        if (EPI == EPI_F32) tma_prefetch_desc(&tm_out);
+        tma_prefetch_desc(&tm_out);
     }
     if (warp == 1) {
         tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
@@ -315,7 +318,7 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
                 if (EPI == EPI_RELU2) {
 #pragma unroll
                     for (int c = 0; c < 64; ++c) {
-                        const float x0 = f[c].x > 0.0f ? f[c].x : 0.0f, x1 = f[c].y > 0.0f ? f[c].y : 0.0f;
+                        const float x0 = fmaxf(f[c].x, 0.0f), x1 = fmaxf(f[c].y, 0.0f);   // NaN -> 0, as x > 0 ? x : 0
                         f[c] = __fmul2_rn(make_float2(x0, x1), make_float2(x0, x1));
                     }
                 } else if (t < a.T) {
@@ -341,21 +344,44 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
                 }
                 const float amax = fmaxf(ax[lane], ax[32 + lane]);
                 ++uc;
-                if (t < a.T) {
+                // the codes go to the warp's 4 KB box (row `lane`, 16-byte chunk c at c ^ (lane % 8), the
+                // 128-byte swizzle) and leave by one TMA store, which drains while the warp folds the
+                // next tile (rows past T are clipped by the tensor map)
+                {
                     const float inv = act_inv(amax);
                     const bool fast = isfinite(inv);
-                    uint4 * q = (uint4 *) (a.qout + (size_t) t * a.N + nc);
+                    uint8_t * cbox = (uint8_t *) so + (warp - 2) * 4096;
+                    if (lane == 0) bulk_wait_read();                        // the previous box has been read
+                    __syncwarp();
+                    if (__all_sync(0xffffffffu, fast)) {          // the usual case, without the per-value branch
 #pragma unroll
-                    for (int c4 = 0; c4 < 8; ++c4) {
-                        const float2 * g = &f[8 * c4];
-                        q[c4] = make_uint4(pack_codes(g[0].x, g[0].y, g[1].x, g[1].y, inv, fast),
+                        for (int c4 = 0; c4 < 8; ++c4) {
+                            const float2 * g = &f[8 * c4];
+                            *(uint4 *) (cbox + lane * 128 + 16 * (c4 ^ (lane & 7))) =
+                                make_uint4(pack_fast(g[0].x, g[0].y, g[1].x, g[1].y, inv),
+                                           pack_fast(g[2].x, g[2].y, g[3].x, g[3].y, inv),
+                                           pack_fast(g[4].x, g[4].y, g[5].x, g[5].y, inv),
+                                           pack_fast(g[6].x, g[6].y, g[7].x, g[7].y, inv));
+                        }
+                    } else {
+#pragma unroll
+                        for (int c4 = 0; c4 < 8; ++c4) {
+                            const float2 * g = &f[8 * c4];
+                            *(uint4 *) (cbox + lane * 128 + 16 * (c4 ^ (lane & 7))) =
+                                make_uint4(pack_codes(g[0].x, g[0].y, g[1].x, g[1].y, inv, fast),
                                            pack_codes(g[2].x, g[2].y, g[3].x, g[3].y, inv, fast),
                                            pack_codes(g[4].x, g[4].y, g[5].x, g[5].y, inv, fast),
                                            pack_codes(g[6].x, g[6].y, g[7].x, g[7].y, inv, fast));
+                        }
                     }
-                    if (halfc == 0) a.sqout[(size_t) t * (a.N / 256) + n0 / 256] = act_scale(amax);
+                    if (t < a.T && halfc == 0) a.sqout[(size_t) t * (a.N / 256) + n0 / 256] = act_scale(amax);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tm_out, nc, m0 + 32 * quad, smem_u32(cbox));
+                        bulk_commit();
+                    }
                 }
-                __syncwarp();
                 continue;
             }
             if (nc < a.N) {
@@ -555,9 +581,9 @@ static int linear_q(int op, const int8_t * xq, const float * sx, int T, const in
     if (((uintptr_t) xq & 15) || ((uintptr_t) w8 & 15) || ((uintptr_t) sw & 15) || ((uintptr_t) q & 15))
         return NXK_EINVAL;
     if (T == 0) return NXK_OK;
-    CUtensorMap ma, mb, mo;
-    memset(&mo, 0, sizeof(mo));                       // no fp32 output: the map is never used
-    if (!make_map(&ma, xq, (uint64_t) T, (uint64_t) K, BM) || !make_map(&mb, w8, (uint64_t) N, (uint64_t) K, BN)) {
+    CUtensorMap ma, mb, mo;                           // mo: the codes, T x N bytes in boxes of 32 rows x 128
+    if (!make_map(&ma, xq, (uint64_t) T, (uint64_t) K, BM) || !make_map(&mb, w8, (uint64_t) N, (uint64_t) K, BN) ||
+        !make_map(&mo, q, (uint64_t) T, (uint64_t) N, 32)) {
         fprintf(stderr, "nexterabert: int8 GEMM tensor map rejected (T %d, K %d, N %d)\n", T, K, N);
         return NXK_ELAUNCH;
     }
