@@ -283,10 +283,9 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
                 const bool live = nc < a.N;                                // columns past N (N % 64 == 0)
                 const float sxb = t < a.T ? sxs[row * a.n_blk + b] : 0.0f;
                 const float2 sx2 = make_float2(sxb, sxb);
-                const float2 nmagic = make_float2(-12582912.0f, -12582912.0f);   // x - m == x + (-m) exactly
                 const float4 * swp = (const float4 *) (sws + b * BN);
                 // f = fma(float(S) * sx, sw, f) per column, two columns per packed instruction, 16 columns
-                // per TMEM load; float(S) exact via the 1.5 * 2^23 bias (|S| <= 2^22).  (Ten warps put
+                // per TMEM load; float(S) is exact (|S| <= 2^22 < 2^24).  (Ten warps put
                 // three on one SM sub-partition, whose 16K registers then allow 168 per thread.)
 #pragma unroll
                 for (int q8 = 0; q8 < 8; ++q8) {
@@ -297,10 +296,8 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
 #pragma unroll
                     for (int c4 = 0; c4 < 4; ++c4) {
                         const float4 w = swp[4 * q8 + c4];
-                        const float2 s0 = __fadd2_rn(make_float2(__int_as_float((int) r[4 * c4] + 0x4B400000),
-                                                                 __int_as_float((int) r[4 * c4 + 1] + 0x4B400000)), nmagic);
-                        const float2 s1 = __fadd2_rn(make_float2(__int_as_float((int) r[4 * c4 + 2] + 0x4B400000),
-                                                                 __int_as_float((int) r[4 * c4 + 3] + 0x4B400000)), nmagic);
+                        const float2 s0 = make_float2(__int2float_rn((int) r[4 * c4]), __int2float_rn((int) r[4 * c4 + 1]));
+                        const float2 s1 = make_float2(__int2float_rn((int) r[4 * c4 + 2]), __int2float_rn((int) r[4 * c4 + 3]));
                         f[8 * q8 + 2 * c4]     = __ffma2_rn(__fmul2_rn(s0, sx2), make_float2(w.x, w.y), f[8 * q8 + 2 * c4]);
                         f[8 * q8 + 2 * c4 + 1] = __ffma2_rn(__fmul2_rn(s1, sx2), make_float2(w.z, w.w), f[8 * q8 + 2 * c4 + 1]);
                     }
