@@ -190,9 +190,13 @@ NEXTERA_API int nxk_attention_kv(const float * q, const float * k, const float *
  * inside the library (2.5 MiB on each device that loads it, kept until exit):
  * at most 131072 query tiles per call, i.e. sum over documents of
  * ceil(len / 32) <= 131072; larger batches return NXK_EINVAL.  h_doc_len is the
- * host copy of doc_len.  The array's device address is looked up on the first
- * call made with each device current, so make that first call before any stream
- * capture.  Calls share the array: two calls in flight at the same time race. */
+ * host copy of doc_len and must equal it; the documents must lie in [0, T)
+ * (a host total above T returns NXK_EINVAL; a device copy that disagrees leaves
+ * the output unwritten and sets error word 0x301, read by nxk_take_error).  The
+ * array's device address is looked up on the first call made with each device
+ * current, so make that first call before any stream capture; a device reset
+ * (cudaDeviceReset) is not supported afterwards.  Calls share the array: two
+ * calls in flight at the same time race. */
 NEXTERA_API int nxk_attention_noalloc(const float * q, const float * k, const float * v, int T, int H, int G, int D,
                                       int half, const float * scale, const int32_t * doc_start,
                                       const int32_t * doc_len, int n_docs, const int32_t * h_doc_len, float * out,

@@ -633,7 +633,7 @@ void plan(const int32_t * start, const int32_t * len, int n_docs, int half, int 
 
 size_t n_items(const int32_t * len, int n_docs, int qt) {
     size_t n = 0;
-    for (int d = 0; d < n_docs; ++d) n += (size_t) (len[d] + qt - 1) / qt;
+    for (int d = 0; d < n_docs; ++d) n += (size_t) (((long long) len[d] + qt - 1) / qt);
     return n;
 }
 
@@ -763,16 +763,23 @@ int nxk_attention_kv(const float * q, const float * k, const float * v, int T, i
 // the library, held until exit).  One item is one 32-query tile of one
 // document, so a batch may hold at most NOALLOC_MAX_ITEMS tiles (sum over the
 // documents of ceil(len / 32)); larger batches are rejected with NXK_EINVAL and
-// a message.  The plan is written on the device by a small planner kernel from
-// doc_start / doc_len, in document order; every entry the attention kernel
-// reads is written by the same call first, so nothing needs clearing.  All calls
-// share the array: two calls whose work overlaps on the GPU (different streams,
-// no ordering between them) race on it and must not be issued.
+// a message.  The documents must lie inside the T query rows: the host checks
+// that its copy of the lengths sums to at most T, and the planner checks every
+// device-side document against [0, T) and its tile count against the host's.
+// The plan is written on the device by that planner kernel from doc_start /
+// doc_len, in document order; every entry the attention kernel reads is written
+// by the same call first, so nothing needs clearing.  When the device lengths
+// disagree with the host copy, the planner writes empty entries instead and
+// sets the error word that nxk_take_error returns (0x301).  All calls share the
+// array: two calls whose work overlaps on the GPU (different streams, no
+// ordering between them) race on it and must not be issued.
 //
 // Host code cannot use the array's name as a device address; its address is
 // looked up once per device with cudaGetSymbolAddress on the first call made
 // with that device current.  That first call should therefore come before any
-// CUDA stream capture.  No device memory is allocated, and no host memory
+// CUDA stream capture.  The cached address belongs to the device's primary
+// context: after cudaDeviceReset it is stale, so this entry point does not
+// support a reset device.  No device memory is allocated, and no host memory
 // either.
 // ---------------------------------------------------------------------------
 #include <cstdio>
@@ -786,28 +793,56 @@ constexpr int NOALLOC_MAX_DEVICES = 64;
 
 static __device__ __align__(256) Item g_noalloc_items[NOALLOC_MAX_ITEMS];
 
+// this file's device error word (the no-workspace planner found a document it must not plan);
+// nxk_take_error reads it through attn_take_error
+__device__ int g_attn_error;
+constexpr int ERR_NOALLOC_PLAN = 0x301;
+
 // One block: each thread owns a contiguous run of documents, counts their tiles,
 // the block scans the counts, then every thread writes its documents' items.
+// The grid that follows has n_expect blocks, counted on the host from its copy
+// of the lengths.  The plan is written only if the device lengths give that
+// same count and every document lies inside [0, T); otherwise every one of the
+// n_expect entries becomes an empty item (no query rows, no keys) and the error
+// word is set, so no entry is ever written past the array and the attention
+// kernel reads nothing outside the caller's buffers.
 __global__ void __launch_bounds__(1024) plan_kernel(Item * __restrict__ items, const int32_t * __restrict__ doc_start,
-                                                    const int32_t * __restrict__ doc_len, int n_docs, int half) {
-    __shared__ int part[1024];
+                                                    const int32_t * __restrict__ doc_len, int n_docs, int half,
+                                                    int T, int n_expect) {
+    __shared__ long long part[1024];
+    __shared__ int bad;
     const int tid = threadIdx.x, nt = blockDim.x;
+    if (tid == 0) bad = 0;
+    __syncthreads();
     const int per = (n_docs + nt - 1) / nt;
     const int d0 = min(n_docs, tid * per), d1 = min(n_docs, d0 + per);
-    int cnt = 0;
-    for (int d = d0; d < d1; ++d) cnt += (doc_len[d] + QT - 1) / QT;
+    long long cnt = 0;
+    for (int d = d0; d < d1; ++d) {
+        const long long lo = doc_start[d], n = doc_len[d];
+        if (n <= 0 || lo < 0 || lo + n > T) bad = 1;
+        cnt += n > 0 ? (n + QT - 1) / QT : 0;
+    }
     part[tid] = cnt;
     __syncthreads();
     for (int off = 1; off < nt; off <<= 1) {        // inclusive scan (Hillis-Steele)
-        const int add = tid >= off ? part[tid - off] : 0;
+        const long long add = tid >= off ? part[tid - off] : 0;
         __syncthreads();
         part[tid] += add;
         __syncthreads();
     }
-    int o = part[tid] - cnt;
+    if (tid == nt - 1 && part[tid] != n_expect) bad = 1;
+    __syncthreads();
+    if (bad) {
+        if (tid == 0) atomicExch(&g_attn_error, ERR_NOALLOC_PLAN);
+        Item e;
+        e.q0 = e.q1 = e.k0 = e.k1 = e.doc = 0;
+        for (int i = tid; i < n_expect; i += nt) items[i] = e;
+        return;
+    }
+    long long o = part[tid] - cnt;
     for (int d = d0; d < d1; ++d) {
         const int lo = doc_start[d], hi = lo + doc_len[d];
-        for (int q0 = lo; q0 < hi; q0 += QT) {
+        for (int q0 = lo; q0 < hi && o < n_expect; q0 += QT) {
             Item it;
             it.q0 = q0;
             it.q1 = min(hi, q0 + QT);
@@ -841,6 +876,16 @@ Item * noalloc_items() {
 } // namespace attn
 } // namespace nxk
 
+namespace nxk {
+// reads and clears this file's device error word (called by nxk_take_error)
+int attn_take_error() {
+    int v = 0, zero = 0;
+    cudaMemcpyFromSymbol(&v, attn::g_attn_error, sizeof(int));
+    cudaMemcpyToSymbol(attn::g_attn_error, &zero, sizeof(int));
+    return v;
+}
+} // namespace nxk
+
 extern "C" int nxk_attention_noalloc(const float * q, const float * k, const float * v, int T, int H, int G, int D,
                                      int half, const float * scale, const int32_t * doc_start,
                                      const int32_t * doc_len, int n_docs, const int32_t * h_doc_len, float * out,
@@ -850,10 +895,15 @@ extern "C" int nxk_attention_noalloc(const float * q, const float * k, const flo
     const int rep = H / G;
     if (rep != 1 && rep != 2 && rep != 4) return NXK_EINVAL;
     if (T == 0 || n_docs == 0) return NXK_OK;
-    long long n_items = 0;
+    long long n_items = 0, n_rows = 0;
     for (int d = 0; d < n_docs; ++d) {
         if (h_doc_len[d] <= 0) return NXK_EINVAL;
-        n_items += (h_doc_len[d] + QT - 1) / QT;
+        n_rows += h_doc_len[d];
+        n_items += ((long long) h_doc_len[d] + QT - 1) / QT;
+    }
+    if (n_rows > T) {
+        fprintf(stderr, "nxk_attention_noalloc: the documents hold %lld rows, more than T = %d\n", n_rows, T);
+        return NXK_EINVAL;
     }
     if (n_items > NOALLOC_MAX_ITEMS) {
         fprintf(stderr, "nxk_attention_noalloc: %lld query tiles exceed the fixed plan of %d "
@@ -864,7 +914,7 @@ extern "C" int nxk_attention_noalloc(const float * q, const float * k, const flo
     Item * items = noalloc_items();
     if (!items) return NXK_ELAUNCH;
     cudaStream_t s = (cudaStream_t) stream;
-    plan_kernel<<<1, 1024, 0, s>>>(items, doc_start, doc_len, n_docs, half);
+    plan_kernel<<<1, 1024, 0, s>>>(items, doc_start, doc_len, n_docs, half, T, (int) n_items);
     const dim3 grid((unsigned) n_items, (unsigned) G);
     switch (rep) {
         case 1: attn_kernel<1><<<grid, QT * 2, 0, s>>>(q, k, v, out, items, scale, doc_start, doc_len, T, H, half); break;

@@ -22,6 +22,7 @@ namespace nxk {
 
 __device__ int g_error;
 int gemm_take_error();      // gemm_i8.cu
+int attn_take_error();      // attention.cu
 
 constexpr int ROW_THREADS = 256;     // 8 rows per block
 
@@ -715,7 +716,8 @@ int32_t nxk_take_error(void * stream) {
     cudaMemcpyFromSymbol(&v, g_error, sizeof(int));
     cudaMemcpyToSymbol(g_error, &zero, sizeof(int));
     const int g = gemm_take_error();        // the GEMM's own word (cleared as well)
-    return v ? v : g;
+    const int a = attn_take_error();        // the attention planner's word (cleared as well)
+    return v ? v : g ? g : a;
 }
 
 int nxk_quantize(const float * x, int T, int C, int8_t * q, float * sx, void * stream) {

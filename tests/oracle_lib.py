@@ -35,11 +35,17 @@ def ptr(a, t=None):
     return a.ctypes.data_as(ctypes.POINTER(t))
 
 
+def default_ref_dir() -> Path:
+    """The reference checkout: $REF_DIR, else a sibling of this repository named `reference`."""
+    env = os.environ.get("REF_DIR")
+    return Path(env) if env else ORACLE_DIR.parent.parent / "reference"
+
+
 def build_oracle(ref: bool = False) -> None:
     """Runs oracle/Makefile (the reference build only when its sources exist)."""
     import subprocess
     targets = ["all"]
-    ref_dir = os.environ.get("REF_DIR", "/root/reference")
+    ref_dir = os.environ.get("REF_DIR") or str(default_ref_dir())
     if ref and Path(ref_dir, "src", "nexterabert.cpp").exists():
         targets.append("ref")
     subprocess.run(["make", "-s", "-C", str(ORACLE_DIR), f"REF_DIR={ref_dir}", *targets], check=True)

@@ -213,3 +213,16 @@ def test_repeated_shapes_replay_graphs_bit_exact(lib, oracle):
     assert rc == 0 and lib.nextera_debug_launches(m.h) > n0
     m.close()
     fresh.close()
+
+
+@pytest.mark.parametrize("preset", ["F16", "F32"])
+def test_float_encoder_files_are_refused_at_load(lib, capfd, preset):
+    # The reference runs float matrices on ggml's mul_mat (src/nexterabert.cpp:1140-1142); this
+    # build has only the int8 path for encoder linears, so such a file is refused at load: NULL and
+    # a message naming the tensor, as for any other file it cannot run.
+    path = sm.cached_model("tiny", sm.tiny_hparams(), preset, seed=0)
+    h = lib.nextera_load(str(path).encode(), lib.nextera_default_params())
+    err = capfd.readouterr().err
+    assert not h
+    assert "is not a quantized matrix this build can expand to int8" in err
+    assert "'blocks." in err

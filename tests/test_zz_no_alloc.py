@@ -87,3 +87,59 @@ def test_no_alloc_rejects_batches_beyond_its_fixed_plan(lib):
     rc = lib.nxk_attention_noalloc(None, None, None, int(lengths.sum()), 4, 2, 64, -1, None, None, None,
                                    len(lengths), lengths.ctypes.data_as(i32), None, None)
     assert rc == -1
+
+
+def test_no_alloc_accepts_exactly_its_fixed_plan(lib):
+    # 131072 one-row documents fill the plan exactly; a one-key softmax weighs its value row by 1,
+    # so every output row is the value row of its KV head
+    from gpulib import P, dev, host
+    import torch
+    H, G, n = 4, 2, 131072
+    lengths = np.ones(n, np.int32)
+    rng = np.random.default_rng(7)
+    q = rng.standard_normal((n, H * 64)).astype(np.float32)
+    k = rng.standard_normal((G, n, 64)).astype(np.float32)
+    v = rng.standard_normal((G, n, 64)).astype(np.float32)
+    scale = np.full(n, 0.125, np.float32)
+    start = np.arange(n, dtype=np.int32)
+    i32 = ctypes.POINTER(ctypes.c_int32)
+    out = torch.full((n, H * 64), float("nan"), dtype=torch.float32, device="cuda")
+    rc = lib.nxk_attention_noalloc(P(dev(q)), P(dev(k)), P(dev(v)), n, H, G, 64, -1, P(dev(scale)), P(dev(start)),
+                                   P(dev(lengths)), n, lengths.ctypes.data_as(i32), P(out), None)
+    assert rc == 0
+    assert lib.nxk_take_error(None) == 0
+    got = host(out).reshape(n, H, 64)
+    for h in range(H):
+        assert np.array_equal(got[:, h], v[h // (H // G)])
+
+
+def test_no_alloc_rejects_documents_past_T(lib):
+    # the documents hold 10 rows but T says 9: refused on the host, nothing launched
+    lengths = np.array([4, 6], np.int32)
+    i32 = ctypes.POINTER(ctypes.c_int32)
+    rc = lib.nxk_attention_noalloc(None, None, None, 9, 4, 2, 64, -1, None, None, None, len(lengths),
+                                   lengths.ctypes.data_as(i32), None, None)
+    assert rc == -1
+
+
+def test_no_alloc_device_lengths_that_disagree_set_the_error_word(lib):
+    # the device copy of the lengths asks for more tiles than the host copy counted: the planner
+    # writes empty entries, the output stays untouched and the error word reports it
+    from gpulib import P, dev, host
+    import torch
+    H, G = 4, 2
+    h_len = np.array([40, 30], np.int32)
+    d_len = np.array([40, 70], np.int32)          # 70 rows would run past T = 70
+    T = int(h_len.sum())
+    q, k, v, scale = _inputs(3, h_len, H, G)
+    start = np.array([0, 40], np.int32)
+    i32 = ctypes.POINTER(ctypes.c_int32)
+    out = torch.full((T, H * 64), 7.0, dtype=torch.float32, device="cuda")
+    rc = lib.nxk_attention_noalloc(P(dev(q)), P(dev(k)), P(dev(v)), T, H, G, 64, -1, P(dev(scale)), P(dev(start)),
+                                   P(dev(d_len)), 2, h_len.ctypes.data_as(i32), P(out), None)
+    assert rc == 0
+    assert lib.nxk_take_error(None) == 0x301
+    assert np.all(host(out) == 7.0)
+    # the next, consistent call plans and runs normally
+    got, want = _run_both(lib, q, k, v, scale, h_len, H, G, -1)
+    assert np.abs(got - want).max() <= TOL * np.abs(want).max()
