@@ -44,6 +44,12 @@ NEXTERA_API int32_t nxk_take_error(void * stream);
  * word that nxk_take_error returns.  The context stays usable. */
 NEXTERA_API int nxk_selftest_wait(int64_t limit_ns, void * stream);
 
+/* Tensor-pipe rate probe for the int8 GEMM's roofline (no counterpart in the reference): n_ctas
+ * CTAs (one per SM when n_ctas <= the SM count), each issuing iters x 4 tcgen05.mma.kind::i8 of
+ * M 128 x N 256 x K 32 on operands resident in shared memory, with no copies and no epilogue.
+ * Work per launch: 2 * 128 * 256 * 128 * iters * n_ctas int ops.  Time it with events. */
+NEXTERA_API int nxk_i8_mma_rate_probe(int n_ctas, int iters, void * stream);
+
 /* ---- weights: build_i8_weight (:1010-1049), on the device ----
  * blocks: n_out rows of GGUF blocks of `type` (any of F32 F16 BF16 Q4_0 Q4_1
  * Q5_0 Q5_1 Q8_0 Q2_K Q3_K Q4_K Q5_K Q6_K); writes w8, scale and (if not NULL) off. */

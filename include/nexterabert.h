@@ -94,8 +94,8 @@ NEXTERA_API int32_t nextera_encode_segments(struct nextera_context * ctx,
                                             const int32_t * lengths, int32_t n_seqs,
                                             float * hidden, float * pooled, int32_t normalize);
 
-/* Heads (reference: src/nexterabert.h:100-121).  Not on the GPU yet: these
- * return 1 with a message on stderr. */
+/* Heads (reference: src/nexterabert.h:100-121), on the GPU: the encoder, then the
+ * pooler / classifier / MLM transform and decoder.  1 when the file has no such head. */
 NEXTERA_API int32_t nextera_pooler_output(struct nextera_context * ctx,
                                           const int32_t * tokens, const int32_t * token_types,
                                           const int32_t * lengths, int32_t n_seqs, float * out);
@@ -158,6 +158,36 @@ NEXTERA_API int32_t nextera_shard_init(struct nextera_context * ctx, int32_t ran
 NEXTERA_API int32_t nextera_encode_sharded(struct nextera_context * ctx, const int32_t * d_tokens, int32_t n_local,
                                            int32_t n_total, float * d_hidden, float * d_pooled, int32_t normalize,
                                            void * stream);
+
+/* ---- one batch of sequences split over several GPUs (one process per GPU) ----
+ * No counterpart in the reference, which runs on one host.  The reference's batch contract
+ * (src/nexterabert.h:69-84: a sequence's result does not depend on the rest of the batch) lets
+ * the sequences of one batch run on different GPUs: each rank encodes a share of them on its own
+ * model replica, and the pooled rows come back to rank 0 in the batch's order, bit for bit what
+ * one GPU gives.  The ranks are the group of nextera_shard_init; without it the whole batch runs
+ * on this context's device. */
+
+/* The partition every rank uses: part[i] = the rank of sequence i.  Longest-first greedy on an
+ * estimate of each sequence's device time (tokens through the linear layers and row ops, plus
+ * query-tile x key pairs through every attention layer), so the ranks finish together.  Depends
+ * only on the lengths and the model, so all ranks compute the same one.  0 ok, 1 bad input. */
+NEXTERA_API int32_t nextera_partition(const struct nextera_context * ctx, const int32_t * lengths, int32_t n_seqs,
+                                      int32_t n_parts, int32_t * part);
+/* nextera_encode_segments over a batch partitioned across the ranks, pooled output only.  Every
+ * rank calls it with the same host arrays (tokens, token_types (may be NULL), lengths); each
+ * encodes its share and rank 0 receives all pooled rows into `pooled` (n_seqs x n_embd, host
+ * memory; other ranks may pass NULL).  The whole batch is checked on every rank first, and the
+ * ranks agree on the outcome before rows move, so all ranks return the same code. */
+NEXTERA_API int32_t nextera_encode_partitioned(struct nextera_context * ctx, const int32_t * tokens,
+                                               const int32_t * token_types, const int32_t * lengths,
+                                               int32_t n_seqs, float * pooled, int32_t normalize);
+/* Device-resident variant: d_tokens holds only this rank's sequences (those with
+ * nextera_partition(...)[i] == rank, concatenated in batch order) in device memory; lengths is
+ * the whole batch (host memory); rank 0's d_pooled (device, n_seqs x n_embd) receives every
+ * sequence's pooled row in batch order.  Enqueued on `stream`; every rank must call it. */
+NEXTERA_API int32_t nextera_encode_partitioned_device(struct nextera_context * ctx, const int32_t * d_tokens,
+                                                      const int32_t * lengths, int32_t n_seqs, float * d_pooled,
+                                                      int32_t normalize, void * stream);
 
 #ifdef __cplusplus
 }

@@ -516,6 +516,47 @@ __global__ void wait_selftest_kernel(uint64_t limit_ns) {
     if (threadIdx.x == 0 && !mbar_wait_ns(smem_u32(&bar), 0, limit_ns)) atomicExch(&g_gemm_error, ERR_SELFTEST);
 }
 
+// Tensor-pipe rate probe (measurement only): one stage of operands resident in shared memory
+// (zeros), and one thread issuing `iters` x 4 tcgen05.mma.kind::i8 (M 128, N 256, K 32) into the
+// two TMEM accumulators in turn, as the GEMM's MMA warp does, with no copies and no epilogue: the
+// rate the GEMM's tensor work could reach if its operands were always ready.  The last MMA's
+// commit is waited on (bounded) before TMEM is released.
+__global__ void __launch_bounds__(128, 1) mma_rate_kernel(int iters) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ uint32_t tslot;
+    for (int i = threadIdx.x; i < STAGE_BYTES / 16; i += blockDim.x) ((uint4 *) smem)[i] = make_uint4(0, 0, 0, 0);
+    fence_proxy_async_smem();
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bar), 1);
+        fence_barrier_init();
+    }
+    if (threadIdx.x < 32) {
+        tmem_alloc(smem_u32(&tslot), TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tslot;
+    if (threadIdx.x == 0) {
+        const uint32_t abase = smem_u32(smem), bbase = smem_u32(smem + A_BYTES);
+        for (int i = 0; i < iters; ++i) {
+            const uint32_t d = tmem + (uint32_t) (i & 1) * BN;
+#pragma unroll
+            for (int kk = 0; kk < BKB / 32; ++kk)
+                mma_i8(d, sdesc_k_sw128(abase + kk * 32), sdesc_k_sw128(bbase + kk * 32), IDESC, (i > 1 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(smem_u32(&bar));
+        if (!mbar_wait(smem_u32(&bar), 0)) atomicExch(&g_gemm_error, ERR_MMA);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (threadIdx.x < 32) tmem_dealloc(tmem, TMEM_COLS);
+}
+
 } // namespace gemm
 
 int gemm_take_error() {
@@ -620,6 +661,16 @@ int nxk_linear_i8_simt(const int8_t * xq, const float * sx, int T, const int8_t 
 int nxk_selftest_wait(int64_t limit_ns, void * stream) {
     if (limit_ns <= 0 || limit_ns > 1000000000) return NXK_EINVAL;
     nxk::gemm::wait_selftest_kernel<<<1, 32, 0, (cudaStream_t) stream>>>((uint64_t) limit_ns);
+    return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
+}
+
+int nxk_i8_mma_rate_probe(int n_ctas, int iters, void * stream) {
+    using namespace nxk::gemm;
+    if (n_ctas <= 0 || n_ctas > 4096 || iters <= 0 || iters > 1000000) return NXK_EINVAL;
+    const int bytes = STAGE_BYTES + 1024;
+    static std::once_flag once;
+    std::call_once(once, [bytes]() { cudaFuncSetAttribute(mma_rate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes); });
+    mma_rate_kernel<<<n_ctas, 128, bytes, (cudaStream_t) stream>>>(iters);
     return cudaPeekAtLastError() == cudaSuccess ? NXK_OK : NXK_ELAUNCH;
 }
 

@@ -138,6 +138,11 @@ struct nextera_context {
     int shard_rank = 0, shard_world = 1;
     ncclComm_t shard_comm = nullptr;
     DevBuf kv_ext, kv_full;       // K / V with halo rows (band layers), gathered K / V (global, HRA)
+    // one batch partitioned over the ranks (nextera_encode_partitioned*): this rank's token ids, the
+    // pooled rows every rank sends to rank 0 (received there in rank order) and rank 0's row map
+    DevBuf part_tok, part_rows, part_idx;
+    int32_t * h_part_idx = nullptr;
+    size_t h_part_idx_n = 0;
 
     int32_t debug_n_layers = -1;
     profiler prof;
@@ -558,6 +563,7 @@ void nextera_free(struct nextera_context * c) {
     }
     for (auto & m : c->prof.marks) cudaEventDestroy(m.first);
     if (c->h_stage) cudaFreeHost(c->h_stage);
+    if (c->h_part_idx) cudaFreeHost(c->h_part_idx);
     if (c->shard_comm) nxs::nccl().comm_destroy(c->shard_comm);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
@@ -1564,6 +1570,271 @@ int32_t nextera_encode_sharded(struct nextera_context * c, const int32_t * d_tok
     float * hid = nullptr;
     return run_encoder(*c, b, rope0, d_tokens, nullptr, false, (cudaStream_t) stream, d_hidden, d_pooled, normalize,
                        &hid, &sh);
+}
+
+// ---------------------------------------------------------------------------
+// one batch of documents partitioned over ranks
+// ---------------------------------------------------------------------------
+namespace {
+
+// Estimated device time of one document of length L, in units of the per-token work of the linear
+// layers and row ops: that work, plus the attention kernel's work per (row of its 64-query tiles,
+// key in the tile's range) over every attention layer (band, full and, at block level, HRA).  The
+// weight of a tile-key against a token, 3.9e-4 at 16 heads, is the ratio of the two measured on
+// B200 for the 4096-document batch (attention 987 ms over 6.62e9 tile-keys, the rest 651 ms over
+// 1.69e6 tokens).
+double doc_cost(const hparams & hp, int64_t L) {
+    const int64_t QT = nxk::attn::QT3;
+    const int64_t half = std::max(1, hp.swa_window / 2);
+    const int64_t tiles = (L + QT - 1) / QT;
+    double keys = 0.0;
+    for (mixer_type m : hp.block_types) {
+        if (m == MIX_SWA) {
+            for (int64_t i = 0; i < tiles; ++i) {
+                const int64_t q0 = i * QT, q1 = std::min(L, q0 + QT);
+                keys += (double) QT * (double) (std::min(L, q1 + half) - std::max<int64_t>(0, q0 - half));
+            }
+        } else if (m == MIX_ATTN) {
+            keys += (double) tiles * QT * (double) L;
+        } else if (m == MIX_HRA) {
+            const int64_t nb = (L + hp.hra_block - 1) / hp.hra_block;
+            keys += (double) ((nb + QT - 1) / QT) * QT * (double) nb;
+        }
+    }
+    return (double) L + 3.9e-4 * keys * (double) hp.n_head / 16.0;
+}
+
+// The partition of a batch and, for rank 0, where each document's pooled row arrives.
+struct PartPlan {
+    std::vector<int32_t> part;         // rank of each document
+    std::vector<int32_t> mine;         // this rank's documents, in batch order
+    std::vector<int32_t> counts;       // documents per rank
+    std::vector<int32_t> row_of;       // document -> row of the rank-ordered concatenation
+    int64_t my_tokens = 0;
+};
+
+// Longest-first greedy assignment: documents in order of falling cost (ties: batch order), each to
+// the rank with the least cost so far (ties: the lowest rank).  Deterministic, so every rank
+// computes the same partition from the same lengths.
+void partition(const hparams & hp, const int32_t * lengths, int32_t n, int32_t parts, int32_t * part) {
+    std::vector<double> cost((size_t) n);
+    for (int32_t i = 0; i < n; ++i) cost[(size_t) i] = doc_cost(hp, lengths[i]);
+    std::vector<int32_t> order((size_t) n);
+    for (int32_t i = 0; i < n; ++i) order[(size_t) i] = i;
+    std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t b) { return cost[(size_t) a] > cost[(size_t) b]; });
+    std::vector<double> load((size_t) parts, 0.0);
+    for (int32_t i : order) {
+        int32_t best = 0;
+        for (int32_t r = 1; r < parts; ++r)
+            if (load[(size_t) r] < load[(size_t) best]) best = r;
+        part[(size_t) i] = best;
+        load[(size_t) best] += cost[(size_t) i];
+    }
+}
+
+int make_part_plan(const nextera_context & c, const int32_t * lengths, int32_t n, int rank, int world, PartPlan & pp) {
+    if (!lengths || n <= 0) return 1;
+    for (int32_t i = 0; i < n; ++i) {
+        if (lengths[i] <= 0) {
+            fprintf(stderr, "nexterabert: empty sequence in batch\n");
+            return 1;
+        }
+    }
+    pp.part.assign((size_t) n, 0);
+    if (world > 1) partition(c.hp, lengths, n, world, pp.part.data());
+    pp.counts.assign((size_t) world, 0);
+    pp.mine.clear();
+    pp.my_tokens = 0;
+    for (int32_t i = 0; i < n; ++i) {
+        pp.counts[(size_t) pp.part[(size_t) i]]++;
+        if (pp.part[(size_t) i] == rank) {
+            pp.mine.push_back(i);
+            pp.my_tokens += lengths[i];
+        }
+    }
+    std::vector<int32_t> next((size_t) world, 0);
+    for (int r = 1; r < world; ++r) next[(size_t) r] = next[(size_t) r - 1] + pp.counts[(size_t) r - 1];
+    pp.row_of.resize((size_t) n);
+    for (int32_t i = 0; i < n; ++i) pp.row_of[(size_t) i] = next[(size_t) pp.part[(size_t) i]]++;
+    return 0;
+}
+
+// After this rank's forward left its documents' pooled rows in c.pooled (batch order among its
+// own): every rank sends them to rank 0, which receives all ranks' rows in rank order and writes
+// each document's row to d_out in batch order.  Enqueued on s; every rank must call it.
+int gather_pooled(nextera_context & c, const PartPlan & pp, int n_seqs, float * d_out, cudaStream_t s) {
+    const int C = c.hp.n_embd, world = c.shard_world, rank = c.shard_rank;
+    const size_t row = (size_t) C;
+    if (world == 1) {
+        if (d_out != c.pooled.as<float>() &&
+            cudaMemcpyAsync(d_out, c.pooled.p, sizeof(float) * row * (size_t) n_seqs, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+            return 3;
+        return 0;
+    }
+    const nxs::NcclApi & n = nxs::nccl();
+    if (rank == 0) {
+        if (!c.part_rows.reserve(sizeof(float) * row * (size_t) n_seqs) || !c.part_idx.reserve(sizeof(int32_t) * (size_t) n_seqs))
+            return 2;
+        if (c.h_part_idx_n < (size_t) n_seqs) {
+            if (c.h_part_idx) cudaFreeHost(c.h_part_idx);
+            c.h_part_idx = nullptr;
+            c.h_part_idx_n = 0;
+            if (cudaMallocHost((void **) &c.h_part_idx, sizeof(int32_t) * (size_t) n_seqs) != cudaSuccess) {
+                cudaGetLastError();
+                return 2;
+            }
+            c.h_part_idx_n = (size_t) n_seqs;
+        }
+    }
+    float * rows = c.part_rows.as<float>();
+    bool ok = nxs::nccl_ok(n.group_start(), "group start");
+    if (rank == 0) {
+        size_t at = (size_t) pp.counts[0];
+        for (int r = 1; r < world; ++r) {
+            const size_t cnt = (size_t) pp.counts[(size_t) r];
+            if (cnt) ok = ok && nxs::nccl_ok(n.recv(rows + at * row, cnt * row, ncclFloat32, r, c.shard_comm, s), "recv");
+            at += cnt;
+        }
+    } else if (pp.counts[(size_t) rank]) {
+        ok = ok && nxs::nccl_ok(n.send(c.pooled.p, (size_t) pp.counts[(size_t) rank] * row, ncclFloat32, 0, c.shard_comm, s),
+                                "send");
+    }
+    ok = nxs::nccl_ok(n.group_end(), "group end") && ok;
+    if (!ok) return 3;
+    if (rank != 0) return 0;
+    if (pp.counts[0] &&
+        cudaMemcpyAsync(rows, c.pooled.p, sizeof(float) * row * (size_t) pp.counts[0], cudaMemcpyDeviceToDevice, s) !=
+            cudaSuccess)
+        return 3;
+    // the row map as a gather: output row i (document i) takes received row row_of[i]
+    memcpy(c.h_part_idx, pp.row_of.data(), sizeof(int32_t) * (size_t) n_seqs);
+    if (cudaMemcpyAsync(c.part_idx.p, c.h_part_idx, sizeof(int32_t) * (size_t) n_seqs, cudaMemcpyHostToDevice, s) !=
+        cudaSuccess)
+        return 3;
+    ++c.launches;
+    return nxk_gather_rows(rows, C, c.part_idx.as<int32_t>(), n_seqs, d_out, s) == NXK_OK ? 0 : 3;
+}
+
+// This rank's forward over its documents (token ids on the host or the device, in batch order of
+// its own documents), pooled rows into c.pooled.
+int run_part(nextera_context & c, const PartPlan & pp, const int32_t * lengths, const int32_t * tokens,
+             const int32_t * types, bool on_host, int32_t normalize, cudaStream_t s) {
+    if (pp.mine.empty()) return 0;
+    std::vector<int32_t> len;
+    len.reserve(pp.mine.size());
+    for (int32_t i : pp.mine) len.push_back(lengths[i]);
+    Batch b;
+    float rope0 = 0.0f;
+    int rc = prepare(c, tokens, types, len.data(), (int32_t) len.size(), on_host, b, rope0);
+    if (rc) return rc;
+    float * hid = nullptr;
+    return run_encoder(c, b, rope0, tokens, types, on_host, s, nullptr, nullptr, normalize, &hid);
+}
+
+} // namespace
+
+int32_t nextera_partition(const struct nextera_context * c, const int32_t * lengths, int32_t n_seqs, int32_t n_parts,
+                          int32_t * part) {
+    if (!c || !lengths || !part || n_seqs < 0 || n_parts < 1) return 1;
+    for (int32_t i = 0; i < n_seqs; ++i)
+        if (lengths[i] <= 0) return 1;
+    partition(c->hp, lengths, n_seqs, n_parts, part);
+    return 0;
+}
+
+int32_t nextera_encode_partitioned(struct nextera_context * c, const int32_t * tokens, const int32_t * token_types,
+                                   const int32_t * lengths, int32_t n_seqs, float * pooled, int32_t normalize) {
+    if (!c || !tokens) return 1;
+    const auto t0 = std::chrono::steady_clock::now();
+    const int world = c->shard_comm ? c->shard_world : 1, rank = c->shard_comm ? c->shard_rank : 0;
+    const int C = c->hp.n_embd;
+    cudaSetDevice(c->device);
+    PartPlan pp;
+    int rc = make_part_plan(*c, lengths, n_seqs, rank, world, pp);
+    if (rc) return rc;
+    // the whole batch is checked on every rank, so bad input fails on all ranks alike, before any
+    // of them communicates
+    std::vector<int64_t> start((size_t) n_seqs + 1, 0);
+    for (int32_t i = 0; i < n_seqs; ++i) start[(size_t) i + 1] = start[(size_t) i] + lengths[i];
+    const bool use_types = token_types && c->hp.n_types > 0;
+    for (int64_t t = 0; t < start[(size_t) n_seqs]; ++t) {
+        if (tokens[t] < 0 || tokens[t] >= c->hp.n_vocab) {
+            fprintf(stderr, "nexterabert: token id %d out of range\n", tokens[t]);
+            return 1;
+        }
+        if (use_types && (token_types[t] < 0 || token_types[t] >= c->hp.n_types)) {
+            fprintf(stderr, "nexterabert: token type id %d out of range\n", token_types[t]);
+            return 1;
+        }
+    }
+    // this rank's ids (and segment ids) in its documents' batch order
+    std::vector<int32_t> tok, typ;
+    tok.reserve((size_t) pp.my_tokens);
+    if (use_types) typ.reserve((size_t) pp.my_tokens);
+    for (int32_t i : pp.mine) {
+        tok.insert(tok.end(), tokens + start[(size_t) i], tokens + start[(size_t) i + 1]);
+        if (use_types) typ.insert(typ.end(), token_types + start[(size_t) i], token_types + start[(size_t) i + 1]);
+    }
+    rc = run_part(*c, pp, lengths, tok.data(), use_types ? typ.data() : nullptr, true, normalize, c->stream);
+    if (rc == 0 && rank == 0 && !c->part_tok.reserve(sizeof(float) * (size_t) n_seqs * C)) rc = 2;
+    if (rc == 0 && cudaStreamSynchronize(c->stream) != cudaSuccess) {
+        fprintf(stderr, "nexterabert: device error: %s\n", cudaGetErrorString(cudaGetLastError()));
+        rc = 3;
+    }
+    if (rc == 0) {
+        if (int32_t e = nxk_take_error(c->stream)) {
+            fprintf(stderr, "nexterabert: a kernel reported device error 0x%x\n", e);
+            rc = 3;
+        }
+    }
+    collect_profile(*c);
+    // the ranks agree on the outcome (the largest code wins) before rows move
+    if (world > 1) {
+        const nxs::NcclApi & n = nxs::nccl();
+        int32_t * st = c->part_idx.reserve(sizeof(int32_t) * (size_t) std::max(world, n_seqs)) ? c->part_idx.as<int32_t>()
+                                                                                                 : nullptr;
+        std::vector<int32_t> all((size_t) world, 3);
+        if (!st || cudaMemcpy(st + rank, &rc, sizeof(int32_t), cudaMemcpyHostToDevice) != cudaSuccess ||
+            !nxs::nccl_ok(n.all_gather(st + rank, st, 1, ncclInt32, c->shard_comm, c->stream), "all-gather") ||
+            cudaMemcpyAsync(all.data(), st, sizeof(int32_t) * (size_t) world, cudaMemcpyDeviceToHost, c->stream) !=
+                cudaSuccess ||
+            cudaStreamSynchronize(c->stream) != cudaSuccess) {
+            cudaGetLastError();
+            return 3;
+        }
+        for (int32_t x : all) rc = std::max(rc, x);
+    }
+    if (rc) return rc;
+    float * dst = rank == 0 ? c->part_tok.as<float>() : nullptr;
+    rc = gather_pooled(*c, pp, n_seqs, dst, c->stream);
+    if (rc == 0 && rank == 0 && pooled &&
+        cudaMemcpyAsync(pooled, dst, sizeof(float) * (size_t) n_seqs * C, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
+        rc = 3;
+    if (cudaStreamSynchronize(c->stream) != cudaSuccess && rc == 0) {
+        fprintf(stderr, "nexterabert: device error: %s\n", cudaGetErrorString(cudaGetLastError()));
+        rc = 3;
+    }
+    c->last_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    if (c->prof.enabled) {
+        c->prof.total_ms += c->last_ms;
+        c->prof.calls++;
+    }
+    return rc;
+}
+
+int32_t nextera_encode_partitioned_device(struct nextera_context * c, const int32_t * d_tokens, const int32_t * lengths,
+                                          int32_t n_seqs, float * d_pooled, int32_t normalize, void * stream) {
+    if (!c || !d_tokens) return 1;
+    const int world = c->shard_comm ? c->shard_world : 1, rank = c->shard_comm ? c->shard_rank : 0;
+    if (rank == 0 && !d_pooled) return 1;
+    cudaSetDevice(c->device);
+    PartPlan pp;
+    int rc = make_part_plan(*c, lengths, n_seqs, rank, world, pp);
+    if (rc) return rc;
+    cudaStream_t s = (cudaStream_t) stream;
+    rc = run_part(*c, pp, lengths, d_tokens, nullptr, false, normalize, s);
+    if (rc) return rc;
+    return gather_pooled(*c, pp, n_seqs, rank == 0 ? d_pooled : nullptr, s);
 }
 
 int32_t nextera_pooler_output(struct nextera_context * c, const int32_t * tokens, const int32_t * token_types,

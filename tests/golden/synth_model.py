@@ -83,10 +83,14 @@ class HParams:
     pooler: bool = False
     untied_decoder: bool = False
     cls_f16: bool = False
+    # embed a word-level tokenizer.json ("w<id>" words; the special ids as [CLS] [SEP] [PAD] [MASK])
+    # under tokenizer.huggingface.json, as the converter embeds the real one (convert_hf_to_gguf.py:204)
+    tokenizer: bool = False
 
 
 # fields added after the first fixtures: left out of the cache key at their defaults
-_LATE_FIELDS = {"cls_task": "", "n_labels": 0, "pooler": False, "untied_decoder": False, "cls_f16": False}
+_LATE_FIELDS = {"cls_task": "", "n_labels": 0, "pooler": False, "untied_decoder": False, "cls_f16": False,
+                "tokenizer": False}
 POOLED_TASKS = ("sequence-classification", "multiple-choice")
 
 
@@ -354,6 +358,8 @@ def write_model(path: str | os.PathLike, hp: HParams, preset: str, seed: int = 0
     w.add_uint32("tokenizer.ggml.seperator_token_id", hp.sep_id)
     w.add_uint32("tokenizer.ggml.padding_token_id", hp.pad_id)
     w.add_uint32("tokenizer.ggml.mask_token_id", hp.mask_id)
+    if hp.tokenizer:
+        w.add_string("tokenizer.huggingface.json", word_tokenizer_json(hp))
     for name, shape, kind in tensor_specs(hp):
         if kind == "w":
             arr = (0.02 * rng.standard_normal(shape)).astype(np.float32)
@@ -372,6 +378,33 @@ def write_model(path: str | os.PathLike, hp: HParams, preset: str, seed: int = 0
     w.close()
     os.replace(str(path) + ".tmp", path)
     return path
+
+
+def word_tokenizer_json(hp: HParams) -> str:
+    """A Hugging Face tokenizer.json for a synthetic model: whitespace-split words "w<id>" map to
+    their ids, the special ids are [CLS] [SEP] [PAD] [MASK], single texts become [CLS] text [SEP]
+    and pairs [CLS] a [SEP] b [SEP] with segment ids 0 / 1 (the layout of a BERT tokenizer)."""
+    special = {hp.cls_id: "[CLS]", hp.sep_id: "[SEP]", hp.pad_id: "[PAD]", hp.mask_id: "[MASK]"}
+    vocab = {special.get(i, f"w{i}"): i for i in range(hp.n_vocab)}
+    unk = "[PAD]"
+    tok = {
+        "version": "1.0", "truncation": None, "padding": None,
+        "added_tokens": [{"id": i, "content": t, "single_word": False, "lstrip": False, "rstrip": False,
+                          "normalized": False, "special": True} for i, t in sorted(special.items())],
+        "normalizer": None,
+        "pre_tokenizer": {"type": "WhitespaceSplit"},
+        "post_processor": {
+            "type": "TemplateProcessing",
+            "single": [{"SpecialToken": {"id": "[CLS]", "type_id": 0}}, {"Sequence": {"id": "A", "type_id": 0}},
+                       {"SpecialToken": {"id": "[SEP]", "type_id": 0}}],
+            "pair": [{"SpecialToken": {"id": "[CLS]", "type_id": 0}}, {"Sequence": {"id": "A", "type_id": 0}},
+                     {"SpecialToken": {"id": "[SEP]", "type_id": 0}}, {"Sequence": {"id": "B", "type_id": 1}},
+                     {"SpecialToken": {"id": "[SEP]", "type_id": 1}}],
+            "special_tokens": {t: {"id": t, "ids": [i], "tokens": [t]} for i, t in special.items()}},
+        "decoder": None,
+        "model": {"type": "WordLevel", "vocab": vocab, "unk_token": unk},
+    }
+    return json.dumps(tok)
 
 
 def model_cache_dir() -> Path:

@@ -44,6 +44,7 @@ def load_lib(path=None):
     sig = {
         "nxk_take_error": ([vp], ctypes.c_int32),
         "nxk_selftest_wait": ([ctypes.c_int64, vp], c_int),
+        "nxk_i8_mma_rate_probe": ([c_int, c_int, vp], c_int),
         "nxk_expand_weight": ([c_int, vp, c_int, c_int, vp, vp, vp, vp], c_int),
         "nxk_embed": ([c_int, vp, c_int, c_int, vp, c_int, c_int, vp, c_int, vp, vp, vp], c_int),
         "nxk_linear_i8": ([vp, vp, c_int, vp, vp, c_int, c_int, vp, vp, vp], c_int),
@@ -102,6 +103,11 @@ def load_lib(path=None):
         "nextera_shard_init": ([vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_char_p], ctypes.c_int32),
         "nextera_encode_sharded": ([vp, vp, ctypes.c_int32, ctypes.c_int32, vp, vp, ctypes.c_int32, vp],
                                    ctypes.c_int32),
+        "nextera_partition": ([vp, i32p, ctypes.c_int32, ctypes.c_int32, i32p], ctypes.c_int32),
+        "nextera_encode_partitioned": ([vp, i32p, i32p, i32p, ctypes.c_int32, f32p, ctypes.c_int32],
+                                       ctypes.c_int32),
+        "nextera_encode_partitioned_device": ([vp, vp, i32p, ctypes.c_int32, vp, ctypes.c_int32, vp],
+                                              ctypes.c_int32),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

@@ -1,9 +1,9 @@
-"""One sequence encoded by two or four GPUs (nextera_shard_init / nextera_encode_sharded).
+"""One sequence encoded by two, four or eight GPUs (nextera_shard_init / nextera_encode_sharded).
 
 Each rank's rows of the last hidden state and the pooled vector must be bit-identical to the whole
 sequence encoded on one GPU: the token convolutions read their neighbours' halo rows, the band
 attention the neighbours' K / V rows, the full attention (and HRA) every rank's K / V, and the
-pooled sum runs over the ranks in the sequence's order.  Needs two (four) GPUs; skipped otherwise.
+pooled sum runs over the ranks in the sequence's order.  Needs two (four, eight) GPUs; skipped otherwise.
 """
 from __future__ import annotations
 
@@ -53,7 +53,7 @@ def _run_ranks(model_path: Path, tokens: np.ndarray, world: int):
     return sorted(results)
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("which", ["tiny", "full"])
 def test_sharded_sequence_matches_one_gpu(which, world):
     if _gpus() < world:
