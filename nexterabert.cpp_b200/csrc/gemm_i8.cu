@@ -667,7 +667,8 @@ int nxk_selftest_wait(int64_t limit_ns, void * stream) {
 int nxk_i8_mma_rate_probe(int n_ctas, int iters, void * stream) {
     using namespace nxk::gemm;
     if (n_ctas <= 0 || n_ctas > 4096 || iters <= 0 || iters > 1000000) return NXK_EINVAL;
-    const int bytes = STAGE_BYTES + 1024;
+    // more shared memory than two CTAs can hold, so each SM runs one CTA (and owns its TMEM alone)
+    const int bytes = 120 * 1024;
     static std::once_flag once;
     std::call_once(once, [bytes]() { cudaFuncSetAttribute(mma_rate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes); });
     mma_rate_kernel<<<n_ctas, 128, bytes, (cudaStream_t) stream>>>(iters);
