@@ -43,7 +43,10 @@ def gpu():
 
 @pytest.fixture(scope="module")
 def cls_model():
-    hp = sm.tiny_hparams(cls_task="sequence-classification", n_labels=3, pooler=True, tokenizer=True)
+    # the CLI's --bench draws ids from [1000, min(vocab, 40000)) (tools/cli.cpp:180), so the file's
+    # vocabulary must exceed 1000 ids
+    hp = sm.tiny_hparams(n_vocab=4096, cls_task="sequence-classification", n_labels=3, pooler=True,
+                         tokenizer=True)
     return sm.cached_model("tiny_front", hp, "Q4_K_M", seed=21)
 
 
