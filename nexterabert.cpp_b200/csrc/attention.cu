@@ -282,21 +282,21 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
 
-// Pass-1 key tile: key row j (64 floats) keeps the two dims 8r + 2m, 8r + 2m + 1 at
-// m * 16 + (((r >> 1) ^ f) << 2) + ((r & 1) << 1), f = ((m >> 1) & 1) | (((j >> 1) & 1) << 1):
-// a thread's 16-byte load (key j, lane pair m, r = 2c, 2c + 1) and those of the 7 other
-// (m, key) combinations of its warp fall in 8 distinct 16-byte bank groups.
+// Pass-1 key tile: key row j at j * KROW floats; in it the two dims 8r + 2m, 8r + 2m + 1 at
+// (4 * (r >> 1) + m) * 4 + 2 * (r & 1).  A thread's 16-byte load (key j, lane pair m, r = 2c, 2c + 1)
+// is then in 16-byte bank group (2j + 4c + m) mod 8 (a row is 18 groups), and the loads of a warp's
+// 8 (m, key 2kg + jj) combinations fall in 8 distinct groups: one conflict-free wavefront.
+constexpr int KROW = 72;
 __device__ __forceinline__ int kpos(int j, int m, int r) {
-    const int f = ((m >> 1) & 1) | (((j >> 1) & 1) << 1);
-    return j * D + m * 16 + ((((r >> 1) ^ f) & 3) << 2) + ((r & 1) << 1);
+    return j * KROW + (4 * (r >> 1) + m) * 4 + 2 * (r & 1);
 }
 
 template <int REP>
 constexpr int tiled_smem_floats() {
-    // Qs [REP * D][QT3] + two key tiles [KT][D] (pass 1); the pass-3 ring of two stages of
-    // [KT][D] values and [KT][QT3 * REP] weights lies over exactly that space; then the maxima and
-    // the reciprocal sums [QT3 * REP] each
-    return REP * D * QT3 + 2 * KT * D + 2 * QT3 * REP;
+    // Qs [REP * D][QT3] + two key tiles [KT][KROW] (pass 1); the pass-3 ring of two stages of
+    // [KT][D] values and [KT][QT3 * REP] weights lies over that space; then the maxima and the
+    // reciprocal sums [QT3 * REP] each
+    return REP * D * QT3 + 2 * KT * KROW + 2 * QT3 * REP;
 }
 
 template <int REP>
@@ -308,22 +308,27 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
                   float * __restrict__ scratch, int slot_keys) {
     constexpr int NT = 128 * REP;
     constexpr int NQH = QT3 * REP;                                  // (query, head) pairs of a unit
-    static_assert(2 * (KT * D + KT * NQH) == REP * D * QT3 + 2 * KT * D, "pass-3 ring = passes 1-2 area");
+    static_assert(2 * (KT * D + KT * NQH) <= REP * D * QT3 + 2 * KT * KROW, "pass-3 ring inside passes 1-2 area");
     extern __shared__ __align__(16) float smem[];
     float (*Qs)[QT3] = reinterpret_cast<float (*)[QT3]>(smem);                       // [REP * D][QT3]
-    float * Kt = smem + REP * D * QT3;                                              // [2][KT * D]
-    float * mx = smem + REP * D * QT3 + 2 * KT * D;                                 // [NQH]
+    float * Kt = smem + REP * D * QT3;                                              // [2][KT * KROW]
+    float * mx = smem + REP * D * QT3 + 2 * KT * KROW;                              // [NQH]
     float * invs = mx + NQH;                                                        // [NQH]
     float * sc_base = scratch + (size_t) blockIdx.x * slot_keys * NQH;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int hq = warp >> 2, w4 = warp & 3;                       // head, and 16 queries of it
     const int qw = 16 * w4;                                        // the warp's first query
-    // pass 1: lane pair m, key group kg (keys 2kg, 2kg + 1 of a step), 4 queries from qa
+    // pass 1: lane pair m, key group kg (keys 2kg, 2kg + 1 of a step), 4 queries from qa.  The
+    // thread keeps the queries it finishes in slots 0-1 and the key it finishes in slot 0, so the
+    // shuffle rounds need no selects: slot i holds query qa + (i ^ 2 * (m >> 1)), slot jj key
+    // 2kg + (jj ^ (m & 1)) of the step.
     const int m = lane & 3, kg = (lane >> 2) & 1;
     const int qa = qw + 4 * (lane >> 3);
     const int qf = qa + 2 * (m >> 1);                              // the 2 queries it finishes
     const int jf = 2 * kg + (m & 1);                               // and the key of a step
+    const int kx0 = (2 * kg + (m & 1)) * KROW + 4 * m;             // slot 0 / 1 key rows, lane pair m
+    const int kx1 = (2 * kg + ((m & 1) ^ 1)) * KROW + 4 * m;
     // pass 2: the pair
     const int p_qh = tid >> 1, p_sub = tid & 1;
     const int p_h = p_qh / QT3, p_qi = p_qh % QT3;
@@ -365,7 +370,7 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
 
         // pass-1 key tile kt -> buffer b: 8-byte pieces, zeros past k1
         auto issue_k = [&](int kt, int b) {
-            float * dst = Kt + b * KT * D;
+            float * dst = Kt + b * KT * KROW;
 #pragma unroll
             for (int z = 0; z < KT * D / 2 / NT; ++z) {
                 const int i = tid + z * NT, j = i >> 5, d = 2 * (i & 31);
@@ -393,15 +398,20 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
         __syncthreads();
 
         // ---- pass 1
-        float2 qv[4][8];                                           // [query][r]: dims 8r + 2m, 8r + 2m + 1
+        float2 qv[4][8];                                           // [slot][r]: dims 8r + 2m, 8r + 2m + 1
+        {
+            const bool sw = (m & 2) != 0;                          // slots 0-1 hold queries qa + 2, qa + 3
 #pragma unroll
-        for (int r = 0; r < 8; ++r) {
-            const float4 a0 = *(const float4 *) &Qs[hq * D + 8 * r + 2 * m][qa];
-            const float4 a1 = *(const float4 *) &Qs[hq * D + 8 * r + 2 * m + 1][qa];
-            qv[0][r] = make_float2(a0.x, a1.x);
-            qv[1][r] = make_float2(a0.y, a1.y);
-            qv[2][r] = make_float2(a0.z, a1.z);
-            qv[3][r] = make_float2(a0.w, a1.w);
+            for (int r = 0; r < 8; ++r) {
+                const float4 a0 = *(const float4 *) &Qs[hq * D + 8 * r + 2 * m][qa];
+                const float4 a1 = *(const float4 *) &Qs[hq * D + 8 * r + 2 * m + 1][qa];
+                const float2 p0 = make_float2(a0.x, a1.x), p1 = make_float2(a0.y, a1.y);
+                const float2 p2 = make_float2(a0.z, a1.z), p3 = make_float2(a0.w, a1.w);
+                qv[0][r] = sw ? p2 : p0;
+                qv[1][r] = sw ? p3 : p1;
+                qv[2][r] = sw ? p0 : p2;
+                qv[3][r] = sw ? p1 : p3;
+            }
         }
         int lo2[2], hi2[2], fe2[2];
         float ml[2] = {-INFINITY, -INFINITY};
@@ -420,54 +430,46 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
                 cp_async_wait<0>();
             }
             __syncthreads();
-            const float * Kb = Kt + buf * KT * D;
+            const float * Kb = Kt + buf * KT * KROW;
+            // the 4-key steps that some query of this warp sees (warp-uniform bounds)
+            const int s_lo = max(0, w_lo - kt) & ~3, s_hi = min(nk, w_hi - kt);
+            const float * k0p = Kb + kx0 + s_lo * KROW, * k1p = Kb + kx1 + s_lo * KROW;
+            float * stp = sc_base + (size_t) (kt - it.k0 + s_lo + jf) * NQH + hq * QT3 + qf;
 #pragma unroll 1
-            for (int s4 = 0; s4 < nk; s4 += 4) {
-                const int kk0 = kt + s4;
-                if (kk0 >= w_hi || kk0 + 4 <= w_lo) continue;      // warp-uniform: no query of the warp sees them
+            for (int s4 = s_lo; s4 < s_hi; s4 += 4, k0p += 4 * KROW, k1p += 4 * KROW, stp += 4 * NQH) {
                 float2 acc[4][2];
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
-                    float4 kv[2];
-#pragma unroll
-                    for (int jj = 0; jj < 2; ++jj) kv[jj] = *(const float4 *) (Kb + kpos(s4 + 2 * kg + jj, m, 2 * c));
+                    const float4 ka = *(const float4 *) (k0p + 16 * c);
+                    const float4 kb = *(const float4 *) (k1p + 16 * c);
 #pragma unroll
                     for (int rr = 0; rr < 2; ++rr) {
                         const int r = 2 * c + rr;
+                        const float2 k0 = rr ? make_float2(ka.z, ka.w) : make_float2(ka.x, ka.y);
+                        const float2 k1 = rr ? make_float2(kb.z, kb.w) : make_float2(kb.x, kb.y);
 #pragma unroll
-                        for (int jj = 0; jj < 2; ++jj) {
-                            const float2 kk = rr ? make_float2(kv[jj].z, kv[jj].w) : make_float2(kv[jj].x, kv[jj].y);
-#pragma unroll
-                            for (int i = 0; i < 4; ++i)
-                                acc[i][jj] = r == 0 ? __fmul2_rn(qv[i][r], kk) : __ffma2_rn(qv[i][r], kk, acc[i][jj]);
+                        for (int i = 0; i < 4; ++i) {
+                            acc[i][0] = r == 0 ? __fmul2_rn(qv[i][r], k0) : __ffma2_rn(qv[i][r], k0, acc[i][0]);
+                            acc[i][1] = r == 0 ? __fmul2_rn(qv[i][r], k1) : __ffma2_rn(qv[i][r], k1, acc[i][1]);
                         }
                     }
                 }
-                // tree level 1 in the thread: a_2m + a_2m+1
-                float t0[4], t1[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    t0[i] = __fadd_rn(acc[i][0].x, acc[i][0].y);
-                    t1[i] = __fadd_rn(acc[i][1].x, acc[i][1].y);
-                }
-                // level 2 with m ^ 1 ((a0+a1) + (a2+a3), (a4+a5) + (a6+a7)): keep key m & 1
-                const bool odd = (m & 1) != 0;
+                // tree level 1 in the thread (a_2m + a_2m+1); level 2 with m ^ 1 ((a0+a1) + (a2+a3),
+                // (a4+a5) + (a6+a7)): slot 0 is the key kept, the partner's slot 1 is that same key;
+                // level 3 with m ^ 2: slots 0-1 are the queries kept, the partner's slots 2-3 the same
                 float u2[4];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    const float keep = odd ? t1[i] : t0[i], send = odd ? t0[i] : t1[i];
+                    const float keep = __fadd_rn(acc[i][0].x, acc[i][0].y);
+                    const float send = __fadd_rn(acc[i][1].x, acc[i][1].y);
                     u2[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 1));
                 }
-                // level 3 with m ^ 2: keep queries 2 * (m >> 1), + 1
-                const bool hi_q = (m & 2) != 0;
                 float sv[2];
 #pragma unroll
-                for (int x = 0; x < 2; ++x) {
-                    const float keep = hi_q ? u2[2 + x] : u2[x], send = hi_q ? u2[x] : u2[2 + x];
-                    sv[x] = __fmul_rn(__fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 2)), sc);
-                }
+                for (int x = 0; x < 2; ++x)
+                    sv[x] = __fmul_rn(__fadd_rn(u2[x], __shfl_xor_sync(0xffffffffu, u2[2 + x], 2)), sc);
                 // stored: the score inside the query's key range, 0 outside (pass 3 reads them as weights)
-                const int kj = kk0 + jf;
+                const int kj = kt + s4 + jf;
                 if (s4 + jf < nk) {
                     float2 st;
                     st.x = kj >= lo2[0] && kj < hi2[0] ? sv[0] : 0.0f;
@@ -475,7 +477,7 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
 #pragma unroll
                     for (int x = 0; x < 2; ++x)
                         if (kj >= lo2[x] && kj < fe2[x]) ml[x] = (ml[x] < sv[x]) ? sv[x] : ml[x];
-                    *(float2 *) (sc_base + (size_t) (kj - it.k0) * NQH + hq * QT3 + qf) = st;
+                    *(float2 *) stp = st;
                 }
             }
             __syncthreads();                                       // buffer buf is free again
