@@ -243,29 +243,21 @@ attn_kernel(const float * __restrict__ q, const float * __restrict__ k, const fl
 // attn_kernel; what changes is which thread does which operation.  A work unit
 // is (64-query tile, KV head g) with the H/G query heads that share g; its
 // scores live in a per-CTA scratch slot in global memory, [key - k0][query,
-// head].  Each warp owns 16 consecutive queries of one head in all three passes,
-// and skips the keys none of them sees (band layers).
-//   pass 1  every score once.  A thread owns 4 of its warp's queries x 2 keys of
-//           a 4-key step, and lanes 2m, 2m + 1 of the 8 lane chains of
-//           NEXTERA_DOT64 (dims 8r + 2m, 8r + 2m + 1): both chains advance in one
-//           packed f32x2 multiply-add per r.  Its queries' values stay in
-//           registers for the whole unit; keys come from shared memory, two r of
-//           one key per 16-byte load.  The tree ((a0+a1)+(a2+a3)) +
-//           ((a4+a5)+(a6+a7)) is then a_2m + a_2m+1 inside the thread and two
-//           shuffle rounds over the four threads of a key (m xor 1, m xor 2),
-//           each halving what a thread keeps, so a thread ends with 2 queries x 1
-//           key of finished scores.  Key tiles arrive by cp.async in 8-byte
-//           pieces, double buffered, in a layout where every load of a warp is
-//           one conflict-free 128-byte wavefront.  The maxima over the keys in
-//           whole groups go to shared memory.
+// head], L2-resident for the band layers.
+//   pass 1  every score once, in register tiles: a thread owns 4 queries x 4
+//           keys and runs the 8 lane chains of NEXTERA_DOT64 one lane after
+//           the other (dims l, 8 + l, ..., 56 + l), folding each finished lane
+//           into the full-group tree ((a0+a1)+(a2+a3)) + ((a4+a5)+(a6+a7)) as
+//           it completes.  Queries and keys sit transposed in shared memory
+//           ([dim][query], [dim][key]), so one float4 of each feeds 16 FMAs.
+//           Partial maxima over the keys in whole groups go to shared memory.
 //   pass 2  two threads per (query, head): the tail keys (the n % 8 after the
 //           last whole group) are recomputed with the hsum256 tree, then the
 //           exp-sum runs with lanes 0-3 of every group on one thread and lanes
 //           4-7 on the other, each exp written over its score; 1 / sum.
-//   pass 3  a thread owns 4 queries x 8 dims (4l .. 4l + 3 and 32 + 4l ..):
-//           o = fma(e * inv, v, o) over the keys in order; the tile's weights
-//           are staged in shared memory, zero outside a query's range (fma(0, v,
-//           o) leaves o unchanged).
+//   pass 3  register tiles of 4 queries x 8 dims: o = fma(e * inv, v, o) over
+//           the keys in order; the tile's weights are staged in shared memory,
+//           zero outside a query's range (fma(0, v, o) leaves o unchanged).
 // ---------------------------------------------------------------------------
 
 // 16-byte asynchronous global -> shared copies (both addresses 16-byte aligned)
@@ -273,30 +265,13 @@ __device__ __forceinline__ void cp_async16(void * dst, const void * src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
                  :: "r"((uint32_t) __cvta_generic_to_shared(dst)), "l"(src) : "memory");
 }
-// 8-byte asynchronous copy (both addresses 8-byte aligned); src_bytes = 0 fills zeros
-__device__ __forceinline__ void cp_async8(void * dst, const void * src, uint32_t src_bytes) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;"
-                 :: "r"((uint32_t) __cvta_generic_to_shared(dst)), "l"(src), "r"(src_bytes) : "memory");
-}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
 
-// Pass-1 key tile: key row j at j * KROW floats; in it the two dims 8r + 2m, 8r + 2m + 1 at
-// (4 * (r >> 1) + m) * 4 + 2 * (r & 1).  A thread's 16-byte load (key j, lane pair m, r = 2c, 2c + 1)
-// is then in 16-byte bank group (2j + 4c + m) mod 8 (a row is 18 groups), and the loads of a warp's
-// 8 (m, key 2kg + jj) combinations fall in 8 distinct groups: one conflict-free wavefront.
-constexpr int KROW = 72;
-__device__ __forceinline__ int kpos(int j, int m, int r) {
-    return j * KROW + (4 * (r >> 1) + m) * 4 + 2 * (r & 1);
-}
-
 template <int REP>
 constexpr int tiled_smem_floats() {
-    // Qs [REP * D][QT3] + two key tiles [KT][KROW] (pass 1); the pass-3 ring of two stages of
-    // [KT][D] values and [KT][QT3 * REP] weights lies over that space; then the maxima and the
-    // reciprocal sums [QT3 * REP] each
-    return REP * D * QT3 + 2 * KT * KROW + 2 * QT3 * REP;
+    return REP * D * QT3 + D * KT + KT * D + KT * QT3 * REP + QT3 * REP;
 }
 
 template <int REP>
@@ -308,41 +283,32 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
                   float * __restrict__ scratch, int slot_keys) {
     constexpr int NT = 128 * REP;
     constexpr int NQH = QT3 * REP;                                  // (query, head) pairs of a unit
-    static_assert(2 * (KT * D + KT * NQH) <= REP * D * QT3 + 2 * KT * KROW, "pass-3 ring inside passes 1-2 area");
     extern __shared__ __align__(16) float smem[];
     float (*Qs)[QT3] = reinterpret_cast<float (*)[QT3]>(smem);                       // [REP * D][QT3]
-    float * Kt = smem + REP * D * QT3;                                              // [2][KT * KROW]
-    float * mx = smem + REP * D * QT3 + 2 * KT * KROW;                              // [NQH]
-    float * invs = mx + NQH;                                                        // [NQH]
+    float (*Ks)[KT] = reinterpret_cast<float (*)[KT]>(smem + REP * D * QT3);         // [D][KT]
+    float (*Vs)[D] = reinterpret_cast<float (*)[D]>(smem + REP * D * QT3 + D * KT);  // [KT][D]
+    float (*Cw)[NQH] = reinterpret_cast<float (*)[NQH]>(smem + REP * D * QT3 + 2 * D * KT);   // [KT][NQH]
+    float * mx = &Cw[0][0];                                        // [8][NQH], passes 1-2 only
+    float * invs = smem + REP * D * QT3 + 2 * D * KT + KT * NQH;    // [NQH]
     float * sc_base = scratch + (size_t) blockIdx.x * slot_keys * NQH;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int hq = warp >> 2, w4 = warp & 3;                       // head, and 16 queries of it
-    const int qw = 16 * w4;                                        // the warp's first query
-    // pass 1: lane pair m, key group kg (keys 2kg, 2kg + 1 of a step), 4 queries from qa.  The
-    // thread keeps the queries it finishes in slots 0-1 and the key it finishes in slot 0, so the
-    // shuffle rounds need no selects: slot i holds query qa + (i ^ 2 * (m >> 1)), slot jj key
-    // 2kg + (jj ^ (m & 1)) of the step.
-    const int m = lane & 3, kg = (lane >> 2) & 1;
-    const int qa = qw + 4 * (lane >> 3);
-    const int qf = qa + 2 * (m >> 1);                              // the 2 queries it finishes
-    const int jf = 2 * kg + (m & 1);                               // and the key of a step
-    const int kx0 = (2 * kg + (m & 1)) * KROW + 4 * m;             // slot 0 / 1 key rows, lane pair m
-    const int kx1 = (2 * kg + ((m & 1) ^ 1)) * KROW + 4 * m;
-    // pass 2: the pair
-    const int p_qh = tid >> 1, p_sub = tid & 1;
+    const int hq = warp >> 2, w4 = warp & 3;                       // 4 warps per query head
+    const int qa = 32 * (w4 & 1) + 4 * (lane & 7);                 // the thread's 4 queries
+    const int kb = 16 * (w4 >> 1) + 4 * (lane >> 3);               // pass 1: its 4 keys of a tile
+    const int kgrp = kb >> 2;                                      // 0..7
+    const int db = 32 * (w4 >> 1) + 8 * (lane >> 3);               // pass 3: its 8 dims
+    const int p_qh = tid >> 1, p_sub = tid & 1;                    // pass 2: the pair
     const int p_h = p_qh / QT3, p_qi = p_qh % QT3;
-    // pass 3: 4 queries, 8 dims
-    const int qa3 = qw + 4 * (lane & 3);
-    const int d3 = 4 * (lane >> 2);
+    const int c_qh = tid % NQH;                                    // pass 3: weight column it fills
 
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
         const Item it = items[u / G];
         const int g = u % G;
         const float sc = scale[it.doc];
         const int dlo = doc_start[it.doc], dhi = dlo + doc_len[it.doc];
-        // key row j (relative to query row 0, may be negative) of head g is at kg_ + j * D
-        const float * kg_ = k + ((ptrdiff_t) g * Tk + koff) * D;
+        // key row j (relative to query row 0, may be negative) of head g is at kg + j * D
+        const float * kg = k + ((ptrdiff_t) g * Tk + koff) * D;
         const float * vg = v + ((ptrdiff_t) g * Tk + koff) * D;
         // the key range [lo, hi) of query row q0 + qi (empty past q1)
         auto range = [&](int qi, int & lo, int & hi) {
@@ -355,35 +321,9 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
             }
             if (t >= it.q1) { lo = it.k0; hi = it.k0; }
         };
-        // keys that any of this warp's 16 queries sees: [w_lo, w_hi) (ranges grow with the row)
-        int w_lo = it.k0, w_hi = it.k0;
-        {
-            const int last = min(qw + 15, it.q1 - it.q0 - 1);
-            if (last >= qw) {
-                int l0, h0, l1, h1;
-                range(qw, l0, h0);
-                range(last, l1, h1);
-                w_lo = l0;
-                w_hi = h1;
-            }
-        }
 
-        // pass-1 key tile kt -> buffer b: 8-byte pieces, zeros past k1
-        auto issue_k = [&](int kt, int b) {
-            float * dst = Kt + b * KT * KROW;
-#pragma unroll
-            for (int z = 0; z < KT * D / 2 / NT; ++z) {
-                const int i = tid + z * NT, j = i >> 5, d = 2 * (i & 31);
-                const bool in = kt + j < it.k1;
-                const float * src = kg_ + (ptrdiff_t) (in ? kt + j : it.k0) * D + d;
-                cp_async8(dst + kpos(j, (d & 7) >> 1, d >> 3), src, in ? 8u : 0u);
-            }
-            cp_async_commit();
-        };
-        issue_k(it.k0, 0);
-
-        // queries, transposed (zeros past q1); the previous unit's last reads of this space are
-        // pass 3's, which a barrier closes
+        // queries, transposed (zeros past q1); the previous unit's last reads of Qs
+        // are in pass 2, which a barrier closes
         for (int i = tid; i < REP * QT3 * (D / 4); i += NT) {
             const int qi = i % QT3, r = i / QT3;
             const int h = r / (D / 4), d4 = r % (D / 4);
@@ -395,105 +335,123 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
             Qs[h * D + 4 * d4 + 2][qi] = x.z;
             Qs[h * D + 4 * d4 + 3][qi] = x.w;
         }
-        __syncthreads();
 
         // ---- pass 1
-        float2 qv[4][8];                                           // [slot][r]: dims 8r + 2m, 8r + 2m + 1
-        {
-            const bool sw = (m & 2) != 0;                          // slots 0-1 hold queries qa + 2, qa + 3
+        int lo4[4], hi4[4], fe4[4];
+        float ml[4];
 #pragma unroll
-            for (int r = 0; r < 8; ++r) {
-                const float4 a0 = *(const float4 *) &Qs[hq * D + 8 * r + 2 * m][qa];
-                const float4 a1 = *(const float4 *) &Qs[hq * D + 8 * r + 2 * m + 1][qa];
-                const float2 p0 = make_float2(a0.x, a1.x), p1 = make_float2(a0.y, a1.y);
-                const float2 p2 = make_float2(a0.z, a1.z), p3 = make_float2(a0.w, a1.w);
-                qv[0][r] = sw ? p2 : p0;
-                qv[1][r] = sw ? p3 : p1;
-                qv[2][r] = sw ? p0 : p2;
-                qv[3][r] = sw ? p1 : p3;
+        for (int a = 0; a < 4; ++a) {
+            int lo, hi;
+            range(qa + a, lo, hi);
+            lo4[a] = lo;
+            hi4[a] = hi;
+            fe4[a] = lo + ((hi - lo) & ~7);
+            ml[a] = -INFINITY;
+        }
+        // keys that any of this warp's 32 queries sees: [w_lo, w_hi) (ranges grow with the row)
+        int w_lo = it.k0, w_hi = it.k0;
+        {
+            const int qb = 32 * (w4 & 1);
+            const int last = min(qb + 31, it.q1 - it.q0 - 1);
+            if (last >= qb) {
+                int l0, h0, l1, h1;
+                range(qb, l0, h0);
+                range(last, l1, h1);
+                w_lo = l0;
+                w_hi = h1;
             }
         }
-        int lo2[2], hi2[2], fe2[2];
-        float ml[2] = {-INFINITY, -INFINITY};
+        const float (*Qh)[QT3] = Qs + hq * D;
+        // key tiles: the next tile's rows are loaded into registers while this one is used
+        constexpr int KPT = KT * D / 4 / NT;
+        float4 kp[KPT];
+        auto kload = [&](int kt) {
 #pragma unroll
-        for (int x = 0; x < 2; ++x) {
-            range(qf + x, lo2[x], hi2[x]);
-            fe2[x] = lo2[x] + ((hi2[x] - lo2[x]) & ~7);
-        }
-        int buf = 0;
-        for (int kt = it.k0; kt < it.k1; kt += KT, buf ^= 1) {
+            for (int z = 0; z < KPT; ++z) {
+                const int i = tid + z * NT, j = i % KT, d4 = i / KT;
+                kp[z] = kt + j < it.k1 ? *(const float4 *) (kg + (ptrdiff_t) (kt + j) * D + 4 * d4)
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        };
+        kload(it.k0);
+        for (int kt = it.k0; kt < it.k1; kt += KT) {
             const int nk = min(KT, it.k1 - kt);
-            if (kt + KT < it.k1) {
-                issue_k(kt + KT, buf ^ 1);
-                cp_async_wait<1>();
-            } else {
-                cp_async_wait<0>();
+            __syncthreads();                                       // Ks free; Qs written
+#pragma unroll
+            for (int z = 0; z < KPT; ++z) {
+                const int i = tid + z * NT, j = i % KT, d4 = i / KT;
+                Ks[4 * d4 + 0][j] = kp[z].x;
+                Ks[4 * d4 + 1][j] = kp[z].y;
+                Ks[4 * d4 + 2][j] = kp[z].z;
+                Ks[4 * d4 + 3][j] = kp[z].w;
             }
             __syncthreads();
-            const float * Kb = Kt + buf * KT * KROW;
-            // the 4-key steps that some query of this warp sees (warp-uniform bounds)
-            const int s_lo = max(0, w_lo - kt) & ~3, s_hi = min(nk, w_hi - kt);
-            const float * k0p = Kb + kx0 + s_lo * KROW, * k1p = Kb + kx1 + s_lo * KROW;
-            float * stp = sc_base + (size_t) (kt - it.k0 + s_lo + jf) * NQH + hq * QT3 + qf;
-#pragma unroll 1
-            for (int s4 = s_lo; s4 < s_hi; s4 += 4, k0p += 4 * KROW, k1p += 4 * KROW, stp += 4 * NQH) {
-                float2 acc[4][2];
+            if (kt + KT < it.k1) kload(kt + KT);
+            // a warp whose 32 queries see none of its 16 keys (band layers) only stores zeros
+            const bool live = kt + kb - 4 * (lane >> 3) < w_hi && kt + kb - 4 * (lane >> 3) + 16 > w_lo;
+            float y0123[4][4], x45[4][4], x6[4][4], x01[4][4], x2[4][4], x0[4][4], x4[4][4];
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const float4 ka = *(const float4 *) (k0p + 16 * c);
-                    const float4 kb = *(const float4 *) (k1p + 16 * c);
+            for (int a = 0; a < 4; ++a)
 #pragma unroll
-                    for (int rr = 0; rr < 2; ++rr) {
-                        const int r = 2 * c + rr;
-                        const float2 k0 = rr ? make_float2(ka.z, ka.w) : make_float2(ka.x, ka.y);
-                        const float2 k1 = rr ? make_float2(kb.z, kb.w) : make_float2(kb.x, kb.y);
+                for (int b2 = 0; b2 < 4; ++b2) x0[a][b2] = 0.0f;
+            if (live) {
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            acc[i][0] = r == 0 ? __fmul2_rn(qv[i][r], k0) : __ffma2_rn(qv[i][r], k0, acc[i][0]);
-                            acc[i][1] = r == 0 ? __fmul2_rn(qv[i][r], k1) : __ffma2_rn(qv[i][r], k1, acc[i][1]);
+            for (int l = 0; l < 8; ++l) {
+                float acc[4][4];
+#pragma unroll
+                for (int r = 0; r < 8; ++r) {
+                    const int d = 8 * r + l;
+                    const float4 qv = *(const float4 *) &Qh[d][qa];
+                    const float4 kv = *(const float4 *) &Ks[d][kb];
+                    const float qq[4] = {qv.x, qv.y, qv.z, qv.w};
+                    const float kk[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+                    for (int a = 0; a < 4; ++a)
+#pragma unroll
+                        for (int b2 = 0; b2 < 4; ++b2)
+                            acc[a][b2] = r == 0 ? __fmul_rn(qq[a], kk[b2]) : __fmaf_rn(qq[a], kk[b2], acc[a][b2]);
+                }
+#pragma unroll
+                for (int a = 0; a < 4; ++a)
+#pragma unroll
+                    for (int b2 = 0; b2 < 4; ++b2) {
+                        const float c = acc[a][b2];
+                        switch (l) {
+                            case 0: x0[a][b2] = c; break;
+                            case 1: x01[a][b2] = __fadd_rn(x0[a][b2], c); break;
+                            case 2: x2[a][b2] = c; break;
+                            case 3: y0123[a][b2] = __fadd_rn(x01[a][b2], __fadd_rn(x2[a][b2], c)); break;
+                            case 4: x4[a][b2] = c; break;
+                            case 5: x45[a][b2] = __fadd_rn(x4[a][b2], c); break;
+                            case 6: x6[a][b2] = c; break;
+                            default: {
+                                const float s = __fmul_rn(__fadd_rn(y0123[a][b2],
+                                                                    __fadd_rn(x45[a][b2], __fadd_rn(x6[a][b2], c))), sc);
+                                x0[a][b2] = s;                     // the finished score
+                            }
                         }
                     }
-                }
-                // tree level 1 in the thread (a_2m + a_2m+1); level 2 with m ^ 1 ((a0+a1) + (a2+a3),
-                // (a4+a5) + (a6+a7)): slot 0 is the key kept, the partner's slot 1 is that same key;
-                // level 3 with m ^ 2: slots 0-1 are the queries kept, the partner's slots 2-3 the same
-                float u2[4];
+            }
+            }
+            // stored: the score inside the query's key range, 0 outside (pass 3 reads them as weights)
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float keep = __fadd_rn(acc[i][0].x, acc[i][0].y);
-                    const float send = __fadd_rn(acc[i][1].x, acc[i][1].y);
-                    u2[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 1));
-                }
-                float sv[2];
+            for (int b2 = 0; b2 < 4; ++b2) {
+                const int kj = kt + kb + b2;
+                if (kb + b2 < nk) {
+                    float sv[4];
 #pragma unroll
-                for (int x = 0; x < 2; ++x)
-                    sv[x] = __fmul_rn(__fadd_rn(u2[x], __shfl_xor_sync(0xffffffffu, u2[2 + x], 2)), sc);
-                // stored: the score inside the query's key range, 0 outside (pass 3 reads them as weights)
-                const int kj = kt + s4 + jf;
-                if (s4 + jf < nk) {
-                    float2 st;
-                    st.x = kj >= lo2[0] && kj < hi2[0] ? sv[0] : 0.0f;
-                    st.y = kj >= lo2[1] && kj < hi2[1] ? sv[1] : 0.0f;
-#pragma unroll
-                    for (int x = 0; x < 2; ++x)
-                        if (kj >= lo2[x] && kj < fe2[x]) ml[x] = (ml[x] < sv[x]) ? sv[x] : ml[x];
-                    *(float2 *) stp = st;
+                    for (int a = 0; a < 4; ++a) {
+                        const bool in = kj >= lo4[a] && kj < hi4[a];
+                        sv[a] = in ? x0[a][b2] : 0.0f;
+                        if (kj >= lo4[a] && kj < fe4[a]) ml[a] = (ml[a] < x0[a][b2]) ? x0[a][b2] : ml[a];
+                    }
+                    *(float4 *) (sc_base + (size_t) (kj - it.k0) * NQH + hq * QT3 + qa) =
+                        make_float4(sv[0], sv[1], sv[2], sv[3]);
                 }
             }
-            __syncthreads();                                       // buffer buf is free again
         }
-        // maxima: the threads that finished a query's scores are lanes ^1 and ^4 of each other
 #pragma unroll
-        for (int x = 0; x < 2; ++x) {
-            float o = __shfl_xor_sync(0xffffffffu, ml[x], 1);
-            ml[x] = (ml[x] < o) ? o : ml[x];
-            o = __shfl_xor_sync(0xffffffffu, ml[x], 4);
-            ml[x] = (ml[x] < o) ? o : ml[x];
-        }
-        if ((lane & 5) == 0) {
-            mx[hq * QT3 + qf] = ml[0];
-            mx[hq * QT3 + qf + 1] = ml[1];
-        }
+        for (int a = 0; a < 4; ++a) mx[kgrp * NQH + hq * QT3 + qa + a] = ml[a];
         __syncthreads();
 
         // ---- pass 2
@@ -501,12 +459,17 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
             int lo, hi;
             range(p_qi, lo, hi);
             const int n = hi - lo, fe = lo + (n & ~7);
-            float m2 = mx[p_qh];
+            float m = -INFINITY;
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+                const float x = mx[r * NQH + p_qh];
+                m = (m < x) ? x : m;
+            }
             float * sp = sc_base + p_qh;
             if (p_sub == 0) {
                 // tail keys: hsum256 ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7)), then * scale
                 for (int kj = fe; kj < hi; ++kj) {
-                    const float4 * kr = (const float4 *) (kg_ + (ptrdiff_t) kj * D);
+                    const float4 * kr = (const float4 *) (kg + (ptrdiff_t) kj * D);
                     float a8[8];
 #pragma unroll
                     for (int r = 0; r < 8; ++r) {
@@ -514,20 +477,20 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
                         const float kk[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
 #pragma unroll
                         for (int l = 0; l < 8; ++l) {
-                            const float qq = Qs[p_h * D + 8 * r + l][p_qi];
-                            a8[l] = r == 0 ? __fmul_rn(qq, kk[l]) : __fmaf_rn(qq, kk[l], a8[l]);
+                            const float qv = Qs[p_h * D + 8 * r + l][p_qi];
+                            a8[l] = r == 0 ? __fmul_rn(qv, kk[l]) : __fmaf_rn(qv, kk[l], a8[l]);
                         }
                     }
                     const float tt = __fadd_rn(__fadd_rn(__fadd_rn(a8[0], a8[4]), __fadd_rn(a8[2], a8[6])),
                                                __fadd_rn(__fadd_rn(a8[1], a8[5]), __fadd_rn(a8[3], a8[7])));
                     const float s = __fmul_rn(sc, tt);
                     sp[(size_t) (kj - it.k0) * NQH] = s;
-                    m2 = (m2 < s) ? s : m2;
+                    m = (m < s) ? s : m;
                 }
             }
             {
-                const float o = __shfl_xor_sync(0xffffffffu, m2, 1);
-                m2 = (m2 < o) ? o : m2;
+                const float o = __shfl_xor_sync(0xffffffffu, m, 1);
+                m = (m < o) ? o : m;
             }
             // whole groups: this thread's lanes 4 * sub .. 4 * sub + 3, summed per lane in key order
             float2 vs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};   // lanes (0,1), (2,3) of this thread
@@ -540,7 +503,7 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
                 for (int z = 0; z < 16; ++z) x[z] = gp[(size_t) (8 * (gi + (z >> 2)) + (z & 3)) * NQH];
 #pragma unroll
                 for (int z = 0; z < 16; z += 2) {               // two exps per packed evaluation; s - m <= 0
-                    const float2 e = exp8x2<true>(__fadd2_rn(make_float2(x[z], x[z + 1]), make_float2(-m2, -m2)));
+                    const float2 e = exp8x2<true>(__fadd2_rn(make_float2(x[z], x[z + 1]), make_float2(-m, -m)));
                     vs2[(z >> 1) & 1] = __fadd2_rn(vs2[(z >> 1) & 1], e);
                     gp[(size_t) (8 * (gi + (z >> 2)) + (z & 3)) * NQH] = e.x;
                     gp[(size_t) (8 * (gi + ((z + 1) >> 2)) + ((z + 1) & 3)) * NQH] = e.y;
@@ -550,7 +513,7 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
 #pragma unroll
                 for (int z = 0; z < 4; z += 2) {
                     float * p0 = gp + (size_t) (8 * gi + z) * NQH, * p1 = p0 + NQH;
-                    const float2 e = exp8x2<true>(__fadd2_rn(make_float2(*p0, *p1), make_float2(-m2, -m2)));
+                    const float2 e = exp8x2<true>(__fadd2_rn(make_float2(*p0, *p1), make_float2(-m, -m)));
                     vs2[z >> 1] = __fadd2_rn(vs2[z >> 1], e);
                     *p0 = e.x;
                     *p1 = e.y;
@@ -566,7 +529,7 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
                                       __fadd_rn(__fadd_rn(vs[1], w[1]), __fadd_rn(vs[3], w[3])));
                 for (int kj = fe; kj < hi; ++kj) {
                     float * p = sp + (size_t) (kj - it.k0) * NQH;
-                    const float e = exp_tail(__fsub_rn(*p, m2));
+                    const float e = exp_tail(__fsub_rn(*p, m));
                     sum = __fadd_rn(sum, e);
                     *p = e;
                 }
@@ -577,16 +540,17 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
 
         // ---- pass 3: o = fma(e * inv, v, o) over the keys in order; e is 0 outside a query's range,
         // and fma(0, v, o) leaves o unchanged.  Value rows and exps arrive by cp.async in a 2-stage
-        // ring laid over the shared memory of passes 1-2 (the maxima and invs excepted).
-        float2 o[4][4];                                            // [query][dims 4l, 4l+2, 32+4l, 32+4l+2]
+        // ring laid over the shared memory of passes 1-2 (invs excepted).
+        float2 o[4][4];                                            // [query][dim pair]
 #pragma unroll
         for (int a = 0; a < 4; ++a)
 #pragma unroll
             for (int z = 0; z < 4; ++z) o[a][z] = make_float2(0.0f, 0.0f);
         float inv4[4];
 #pragma unroll
-        for (int a = 0; a < 4; ++a) inv4[a] = invs[hq * QT3 + qa3 + a];
+        for (int a = 0; a < 4; ++a) inv4[a] = invs[hq * QT3 + qa + a];
         constexpr int STAGE = KT * D + KT * NQH;                   // V tile [KT][D], exps [KT][NQH]
+        static_assert(2 * STAGE <= REP * D * QT3 + 2 * D * KT + KT * NQH, "pass-3 ring overlaps invs");
         auto issue = [&](int kt, int st) {
             const int nk = min(KT, it.k1 - kt);
             float * sv = smem + st * STAGE;
@@ -616,12 +580,12 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
             const int jlo = max(0, w_lo - kt), jhi = min(nk, w_hi - kt);
 #pragma unroll 2
             for (int j = jlo; j < jhi; ++j) {
-                const float4 e = *(const float4 *) (se + j * NQH + hq * QT3 + qa3);
+                const float4 e = *(const float4 *) (se + j * NQH + hq * QT3 + qa);
                 const float2 c01 = __fmul2_rn(make_float2(e.x, e.y), make_float2(inv4[0], inv4[1]));
                 const float2 c23 = __fmul2_rn(make_float2(e.z, e.w), make_float2(inv4[2], inv4[3]));
                 const float cc[4] = {c01.x, c01.y, c23.x, c23.y};
-                const float4 v0 = *(const float4 *) (sv + j * D + d3);
-                const float4 v1 = *(const float4 *) (sv + j * D + 32 + d3);
+                const float4 v0 = *(const float4 *) (sv + j * D + db);
+                const float4 v1 = *(const float4 *) (sv + j * D + db + 4);
                 const float2 vv[4] = {make_float2(v0.x, v0.y), make_float2(v0.z, v0.w),
                                       make_float2(v1.x, v1.y), make_float2(v1.z, v1.w)};
 #pragma unroll
@@ -635,11 +599,11 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
         }
 #pragma unroll
         for (int a = 0; a < 4; ++a) {
-            const int t = it.q0 + qa3 + a;
+            const int t = it.q0 + qa + a;
             if (t < it.q1) {
-                float * op = out + ((size_t) t * H + (size_t) g * REP + hq) * D;
-                *(float4 *) (op + d3) = make_float4(o[a][0].x, o[a][0].y, o[a][1].x, o[a][1].y);
-                *(float4 *) (op + 32 + d3) = make_float4(o[a][2].x, o[a][2].y, o[a][3].x, o[a][3].y);
+                float4 * op = (float4 *) (out + ((size_t) t * H + (size_t) g * REP + hq) * D + db);
+                op[0] = make_float4(o[a][0].x, o[a][0].y, o[a][1].x, o[a][1].y);
+                op[1] = make_float4(o[a][2].x, o[a][2].y, o[a][3].x, o[a][3].y);
             }
         }
     }
