@@ -283,6 +283,10 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
                   float * __restrict__ scratch, int slot_keys) {
     constexpr int NT = 128 * REP;
     constexpr int NQH = QT3 * REP;                                  // (query, head) pairs of a unit
+    // pass-2 ring tile (band layers): two stages of [KT2][NQH] over the shared memory of pass 1
+    // (all of it but invs)
+    constexpr int KT2 = 2 * 64 * NQH <= REP * D * QT3 + 2 * D * KT + KT * NQH ? 64 : 32;
+    static_assert(2 * KT2 * NQH <= REP * D * QT3 + 2 * D * KT + KT * NQH, "pass-2 ring overlaps invs");
     extern __shared__ __align__(16) float smem[];
     float (*Qs)[QT3] = reinterpret_cast<float (*)[QT3]>(smem);                       // [REP * D][QT3]
     float (*Ks)[KT] = reinterpret_cast<float (*)[KT]>(smem + REP * D * QT3);         // [D][KT]
@@ -492,31 +496,85 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
                 const float o = __shfl_xor_sync(0xffffffffu, m, 1);
                 m = (m < o) ? o : m;
             }
-            // whole groups: this thread's lanes 4 * sub .. 4 * sub + 3, summed per lane in key order
+            // whole groups: this thread's lanes 4 * sub .. 4 * sub + 3, summed per lane in key order;
+            // each exp is written back over its score
             float2 vs2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};   // lanes (0,1), (2,3) of this thread
             const int ng = n >> 3;
-            float * gp = sp + (size_t) (lo - it.k0 + 4 * p_sub) * NQH;
-            int gi = 0;
-            for (; gi + 4 <= ng; gi += 4) {                        // 16 loads in flight
-                float x[16];
+            if (half < 0) {
+                // full layers (long key ranges): each thread streams its own scores, 16 loads in flight
+                float * gp = sp + (size_t) (lo - it.k0 + 4 * p_sub) * NQH;
+                int gi = 0;
+                for (; gi + 4 <= ng; gi += 4) {
+                    float x[16];
 #pragma unroll
-                for (int z = 0; z < 16; ++z) x[z] = gp[(size_t) (8 * (gi + (z >> 2)) + (z & 3)) * NQH];
+                    for (int z = 0; z < 16; ++z) x[z] = gp[(size_t) (8 * (gi + (z >> 2)) + (z & 3)) * NQH];
 #pragma unroll
-                for (int z = 0; z < 16; z += 2) {               // two exps per packed evaluation; s - m <= 0
-                    const float2 e = exp8x2<true>(__fadd2_rn(make_float2(x[z], x[z + 1]), make_float2(-m, -m)));
-                    vs2[(z >> 1) & 1] = __fadd2_rn(vs2[(z >> 1) & 1], e);
-                    gp[(size_t) (8 * (gi + (z >> 2)) + (z & 3)) * NQH] = e.x;
-                    gp[(size_t) (8 * (gi + ((z + 1) >> 2)) + ((z + 1) & 3)) * NQH] = e.y;
+                    for (int z = 0; z < 16; z += 2) {           // two exps per packed evaluation; s - m <= 0
+                        const float2 e = exp8x2<true>(__fadd2_rn(make_float2(x[z], x[z + 1]), make_float2(-m, -m)));
+                        vs2[(z >> 1) & 1] = __fadd2_rn(vs2[(z >> 1) & 1], e);
+                        gp[(size_t) (8 * (gi + (z >> 2)) + (z & 3)) * NQH] = e.x;
+                        gp[(size_t) (8 * (gi + ((z + 1) >> 2)) + ((z + 1) & 3)) * NQH] = e.y;
+                    }
                 }
-            }
-            for (; gi < ng; ++gi) {
+                for (; gi < ng; ++gi) {
 #pragma unroll
-                for (int z = 0; z < 4; z += 2) {
-                    float * p0 = gp + (size_t) (8 * gi + z) * NQH, * p1 = p0 + NQH;
-                    const float2 e = exp8x2<true>(__fadd2_rn(make_float2(*p0, *p1), make_float2(-m, -m)));
-                    vs2[z >> 1] = __fadd2_rn(vs2[z >> 1], e);
-                    *p0 = e.x;
-                    *p1 = e.y;
+                    for (int z = 0; z < 4; z += 2) {
+                        float * p0 = gp + (size_t) (8 * gi + z) * NQH, * p1 = p0 + NQH;
+                        const float2 e = exp8x2<true>(__fadd2_rn(make_float2(*p0, *p1), make_float2(-m, -m)));
+                        vs2[z >> 1] = __fadd2_rn(vs2[z >> 1], e);
+                        *p0 = e.x;
+                        *p1 = e.y;
+                    }
+                }
+            } else {
+                // band layers (a few hundred keys, where the streamed loads above wait on their
+                // latency): the unit's scores come through a 2-stage cp.async ring of [KT2 keys][NQH]
+                // tiles over the shared memory of pass 1, free once every thread has read the maxima
+                // and finished its tail keys
+                __syncthreads();
+                const int lb = lo + 4 * p_sub;                     // the thread's first key of group 0
+                float * ring = smem;                               // [2][KT2][NQH]
+                auto issue2 = [&](int kt, int st) {
+                    const int nk = min(KT2, it.k1 - kt);
+                    const float * src = sc_base + (size_t) (kt - it.k0) * NQH;
+                    float * dst = ring + st * KT2 * NQH;
+                    for (int i = tid; i < nk * (NQH / 4); i += NT) cp_async16(dst + 4 * i, src + 4 * i);
+                    cp_async_commit();
+                };
+                issue2(it.k0, 0);
+                int st2 = 0;
+                for (int kt = it.k0; kt < it.k1; kt += KT2, st2 ^= 1) {
+                    const int nk = min(KT2, it.k1 - kt);
+                    if (kt + KT2 < it.k1) {
+                        issue2(kt + KT2, st2 ^ 1);
+                        cp_async_wait<1>();
+                    } else {
+                        cp_async_wait<0>();
+                    }
+                    __syncthreads();
+                    const float * se = ring + st2 * KT2 * NQH + p_qh;
+                    // groups i whose keys lb + 8i .. lb + 8i + 3 meet [kt, kt + nk)
+                    const int i0 = max(0, (kt - lb + 4) >> 3);
+                    const int i1 = min(ng, ((kt + nk - 1 - lb) >> 3) + 1);
+                    for (int i = i0; i < i1; ++i) {
+#pragma unroll
+                        for (int z = 0; z < 4; z += 2) {
+                            const int ka = lb + 8 * i + z;
+                            const bool ia = ka >= kt && ka < kt + nk, ib = ka + 1 >= kt && ka + 1 < kt + nk;
+                            const float xa = ia ? se[(ka - kt) * NQH] : m, xb = ib ? se[(ka + 1 - kt) * NQH] : m;
+                            const float2 e = exp8x2<true>(__fadd2_rn(make_float2(xa, xb), make_float2(-m, -m)));
+                            float * gq = sp + (size_t) (ka - it.k0) * NQH;
+                            if (ia) {
+                                vs2[z >> 1].x = __fadd_rn(vs2[z >> 1].x, e.x);
+                                gq[0] = e.x;
+                            }
+                            if (ib) {
+                                vs2[z >> 1].y = __fadd_rn(vs2[z >> 1].y, e.y);
+                                gq[NQH] = e.y;
+                            }
+                        }
+                    }
+                    __syncthreads();
                 }
             }
             // sum = ((v0+v4)+(v2+v6)) + ((v1+v5)+(v3+v7)); lanes 4-7 are the partner's 0-3
