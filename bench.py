@@ -613,10 +613,13 @@ def run_b200(args, rank, world, local_rank, dist):
     top = max(k_ms, key=k_ms.get)
     roof = None
     if rank == 0:
-        i8_peak = int8_peak_tops(torch)
+        i8_peak = i8_mma_peak(torch, L, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
         lin = {"bound": "tensor", "achieved": lin_ops / (k_ms["int8_linear"] * 1e-3) / 1e12, "peak": i8_peak,
                "unit": "TOPS", "kernel": "gemm_i8_tc (int8 linear layers)",
-               "peak_source": "dense int8 GEMM measured in this run (cuBLASLt via torch._int_mm, 8192^3, burst)",
+               "peak_source": "tcgen05 kind::i8 rate measured in this run (nxk_i8_mma_rate_probe: operands "
+                              "resident in shared memory, one CTA per SM, burst)",
+               "library_int8_gemm_tops": int8_peak_tops(torch),
+               "library_source": "cuBLASLt dense int8 (torch._int_mm 8192^3) in this run",
                "algorithmic": "sum over the step's 141-per-token int8 linears of 2*T*N*K"}
         lin["frac"] = lin["achieved"] / lin["peak"]
         f32_peak = fp32_peak_tflops(torch)
