@@ -56,6 +56,16 @@ NEXTERA_API int nxk_i8_mma_rate_probe(int n_ctas, int iters, void * stream);
 NEXTERA_API int nxk_expand_weight(int type, const void * blocks, int n_in, int n_out,
                                   int8_t * w8, float * scale, int32_t * off, void * stream);
 
+/* ---- quantization of fp32 rows into GGUF blocks (the block encoders behind nextera_quantize,
+ * tools/quantize.cpp's ggml_quantize_chunk) ----
+ * x: rows x n_per_row fp32 (device); out: rows x row_size(type) bytes of `type` blocks (F16 Q8_0
+ * Q4_0 Q4_1 Q5_0 Q5_1 Q2_K Q3_K Q4_K Q5_K Q6_K; ggml type ids).  n_per_row must be a multiple of the
+ * block size (32, or 256 for the K-quants).  The legacy types are bit-identical to ggml's reference
+ * quantizers as gguf-py restates them; the K-quants are a direct per-sub-block fit in the published
+ * layouts (valid encodings, not ggml's iterative scale search). */
+NEXTERA_API int nxk_quantize_rows(int type, const float * x, int64_t n_per_row, int64_t rows, void * out,
+                                  void * stream);
+
 /* ---- embedding: ggml_get_rows (+ ggml_add of segment rows), :1272-1273 ----
  * table: n_rows rows of C values in blocks of `type`.  An id outside [0, n_rows)
  * yields a zero row and sets the device error word (ids are checked on the host

@@ -189,6 +189,17 @@ NEXTERA_API int32_t nextera_encode_partitioned_device(struct nextera_context * c
                                                       const int32_t * lengths, int32_t n_seqs, float * d_pooled,
                                                       int32_t normalize, void * stream);
 
+/* ---- the model quantizer (reference: tools/quantize.cpp, a separate program there) ----
+ * Re-encodes the 2-D weights of an F32 / F16 GGUF (in_path) into out_path with the file type
+ * `ftype` (F32 F16 Q8_0 Q6_K Q5_K_M Q5_K_S Q5_0 Q4_K_M Q4_K_S Q4_0 Q3_K_M) and the reference tool's
+ * rules: which tensors are quantized, the "_M" presets' extra bits, the row-size fallback of the
+ * K-quants, and overrides "SUBSTRING=TYPE" (its --tensor-type).  The block encoding runs on the
+ * current CUDA device; the other tensors and every metadata key are copied.  Prints one line per
+ * re-encoded tensor on stdout.  0 ok, 1 bad input or file error, 2 allocation failure, 3 device
+ * failure.  No context is needed. */
+NEXTERA_API int32_t nextera_quantize(const char * in_path, const char * out_path, const char * ftype,
+                                     int32_t n_overrides, const char * const * overrides);
+
 #ifdef __cplusplus
 }
 #endif

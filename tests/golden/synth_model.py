@@ -201,7 +201,66 @@ def quantize_q6_k(x: np.ndarray) -> np.ndarray:
                            d.reshape(nb, 1).view(np.uint8)], axis=1)
 
 
-_K_ENCODERS = {QT.Q4_K: quantize_q4_k, QT.Q5_K: quantize_q5_k, QT.Q6_K: quantize_q6_k}
+def quantize_q2_k(x: np.ndarray) -> np.ndarray:
+    """16 sub-blocks of 16, affine: 4-bit scale and minimum codes under fp16 d / dmin, 2-bit codes."""
+    nb = x.shape[0]
+    xb = x.reshape(nb, 16, 16)
+    lo = np.minimum(xb.min(-1), 0.0)
+    hi = xb.max(-1)
+    scale = (hi - lo) / 3
+    mins = -lo
+    d = _f16(scale.max(-1) / 15.0)
+    dmin = _f16(mins.max(-1) / 15.0)
+    df = d.astype(np.float32)[:, None]
+    dmf = dmin.astype(np.float32)[:, None]
+    with np.errstate(divide="ignore", invalid="ignore"):
+        sc = np.where(df > 0, np.clip(np.rint(scale / df), 0, 15), 0).astype(np.uint8)
+        mq = np.where(dmf > 0, np.clip(np.rint(mins / dmf), 0, 15), 0).astype(np.uint8)
+    dsub = (df * sc.astype(np.float32))[:, :, None]
+    dm = (dmf * mq.astype(np.float32))[:, :, None]
+    with np.errstate(divide="ignore", invalid="ignore"):
+        q = np.where(dsub > 0, np.clip(np.rint((xb + dm) / dsub), 0, 3), 0).astype(np.uint8)
+    q = q.reshape(nb, 2, 4, 32)                          # [half][shift][position]
+    qs = np.zeros((nb, 2, 32), dtype=np.uint8)
+    for k in range(4):
+        qs |= (q[:, :, k, :] << (2 * k)).astype(np.uint8)
+    return np.concatenate([sc | (mq << 4), qs.reshape(nb, 64), d.reshape(nb, 1).view(np.uint8),
+                           dmin.reshape(nb, 1).view(np.uint8)], axis=1)
+
+
+def quantize_q3_k(x: np.ndarray) -> np.ndarray:
+    """16 sub-blocks of 16, symmetric: 6-bit scales (stored + 32) under an fp16 d, 3-bit codes in
+    [-4, 3] stored + 4 (low 2 bits in qs, bit 2 in hmask)."""
+    nb = x.shape[0]
+    xb = x.reshape(nb, 16, 16)
+    s = np.abs(xb).max(-1) / 4.0
+    d = _f16(s.max(-1) / 31.0)
+    df = d.astype(np.float32)[:, None]
+    with np.errstate(divide="ignore", invalid="ignore"):
+        sc = np.where(df > 0, np.clip(np.rint(s / df), -32, 31), 0).astype(np.int16)
+    dsub = (df * sc.astype(np.float32))[:, :, None]
+    with np.errstate(divide="ignore", invalid="ignore"):
+        q = (np.where(dsub != 0, np.clip(np.rint(xb / dsub), -4, 3), 0) + 4).astype(np.uint8)
+    q = q.reshape(nb, 2, 4, 32)
+    hmask = np.zeros((nb, 32), dtype=np.uint8)
+    qs = np.zeros((nb, 2, 32), dtype=np.uint8)
+    for h in range(2):
+        for k in range(4):
+            hmask |= (((q[:, h, k, :] >> 2) & 1) << (4 * h + k)).astype(np.uint8)
+            qs[:, h, :] |= ((q[:, h, k, :] & 3) << (2 * k)).astype(np.uint8)
+    sc6 = (sc + 32).astype(np.uint8)
+    scb = np.zeros((nb, 12), dtype=np.uint8)
+    for j in range(16):
+        if j < 8:
+            scb[:, j] |= sc6[:, j] & 15
+        else:
+            scb[:, j - 8] |= ((sc6[:, j] & 15) << 4).astype(np.uint8)
+        scb[:, 8 + j % 4] |= (((sc6[:, j] >> 4) & 3) << (2 * (j // 4))).astype(np.uint8)
+    return np.concatenate([hmask, qs.reshape(nb, 64), scb, d.reshape(nb, 1).view(np.uint8)], axis=1)
+
+
+_K_ENCODERS = {QT.Q2_K: quantize_q2_k, QT.Q3_K: quantize_q3_k, QT.Q4_K: quantize_q4_k, QT.Q5_K: quantize_q5_k,
+               QT.Q6_K: quantize_q6_k}
 
 
 def quantize_rows(w: np.ndarray, qt) -> np.ndarray:

@@ -104,6 +104,9 @@ def load_lib(path=None):
         "nextera_encode_sharded": ([vp, vp, ctypes.c_int32, ctypes.c_int32, vp, vp, ctypes.c_int32, vp],
                                    ctypes.c_int32),
         "nextera_partition": ([vp, i32p, ctypes.c_int32, ctypes.c_int32, i32p], ctypes.c_int32),
+        "nextera_quantize": ([ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_int32,
+                              ctypes.POINTER(ctypes.c_char_p)], ctypes.c_int32),
+        "nxk_quantize_rows": ([c_int, vp, ctypes.c_int64, ctypes.c_int64, vp, vp], c_int),
         "nextera_encode_partitioned": ([vp, i32p, i32p, i32p, ctypes.c_int32, f32p, ctypes.c_int32],
                                        ctypes.c_int32),
         "nextera_encode_partitioned_device": ([vp, vp, i32p, ctypes.c_int32, vp, ctypes.c_int32, vp],
