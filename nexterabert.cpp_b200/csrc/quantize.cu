@@ -25,7 +25,6 @@
 #include "nexterabert.h"
 #include "nextera_kernels.h"
 
-#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -42,13 +41,23 @@ namespace quant {
 enum : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8, T_Q2_K = 10,
              T_Q3_K = 11, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14 };
 
-__device__ __forceinline__ void put_f16(uint8_t * p, float v) {
-    const __half h = __float2half_rn(v);
-    const uint16_t b = __half_as_ushort(h);
-    p[0] = (uint8_t) (b & 0xff);
-    p[1] = (uint8_t) (b >> 8);
+// fp32 -> fp16 bits, round to nearest even (cvt.rn.f16.f32), widened to 32 bits, and back (exact).
+// The bits are kept in 32-bit registers and leave by one 16-bit store (every fp16 field of a block
+// sits at an even offset, and blocks are an even number of bytes).
+__device__ __forceinline__ uint32_t f16_bits(float v) {
+    uint32_t b;
+    asm("{\n\t.reg .b16 h;\n\tcvt.rn.f16.f32 h, %1;\n\tcvt.u32.u16 %0, h;\n\t}" : "=r"(b) : "f"(v));
+    return b;
 }
-__device__ __forceinline__ float f16r(float v) { return __half2float(__float2half_rn(v)); }
+__device__ __forceinline__ float f16_value(uint32_t b) {
+    float v;
+    asm("{\n\t.reg .b16 h;\n\tcvt.u16.u32 h, %1;\n\tcvt.f32.f16 %0, h;\n\t}" : "=f"(v) : "r"(b));
+    return v;
+}
+__device__ __forceinline__ void put_f16(uint8_t * p, float v) {
+    *reinterpret_cast<unsigned short *>(p) = (unsigned short) f16_bits(v);
+}
+__device__ __forceinline__ float f16r(float v) { return f16_value(f16_bits(v)); }
 __device__ __forceinline__ float safe_inv(float d) { return d == 0.0f ? 0.0f : __fdiv_rn(1.0f, d); }
 
 // index of the first value of largest magnitude (numpy argmax of |x|: first on ties)
@@ -138,7 +147,7 @@ __device__ void affine_k(const float * x, uint8_t * o, uint8_t (&q)[256]) {
         for (int i = 1; i < 32; ++i) { lo = fminf(lo, x[32 * j + i]); hi = fmaxf(hi, x[32 * j + i]); }
         lo = fminf(lo, 0.0f);
         scale[j] = __fdiv_rn(__fsub_rn(hi, lo), (float) LEVELS);
-        mins[j] = -lo;
+        mins[j] = __fsub_rn(0.0f, lo);                  // +0 (not -0) when lo is 0
         smax = fmaxf(smax, scale[j]);
         mmax = fmaxf(mmax, mins[j]);
     }
@@ -226,7 +235,7 @@ __device__ void q2_k(const float * x, uint8_t * o) {
         for (int i = 1; i < 16; ++i) { lo = fminf(lo, x[16 * j + i]); hi = fmaxf(hi, x[16 * j + i]); }
         lo = fminf(lo, 0.0f);
         scale[j] = __fdiv_rn(__fsub_rn(hi, lo), 3.0f);
-        mins[j] = -lo;
+        mins[j] = __fsub_rn(0.0f, lo);                  // +0 (not -0) when lo is 0
         smax = fmaxf(smax, scale[j]);
         mmax = fmaxf(mmax, mins[j]);
     }
@@ -324,7 +333,7 @@ __global__ void f32_to_f16_kernel(const float * __restrict__ x, int64_t n, uint8
 
 __global__ void f16_to_f32_kernel(const uint16_t * __restrict__ x, int64_t n, float * __restrict__ out) {
     const int64_t i = blockIdx.x * (int64_t) blockDim.x + threadIdx.x;
-    if (i < n) out[i] = __half2float(__ushort_as_half(x[i]));
+    if (i < n) out[i] = f16_value(x[i]);
 }
 
 bool supported_target(int t) {

@@ -143,7 +143,7 @@ def _affine_k(x: np.ndarray, levels: int):
     lo = np.minimum(xb.min(-1), 0.0)
     hi = xb.max(-1)
     scale = (hi - lo) / levels
-    mins = -lo
+    mins = 0.0 - lo                                     # +0 (not -0) when lo is 0
     d = _f16(scale.max(-1) / 63.0)
     dmin = _f16(mins.max(-1) / 63.0)
     df = d.astype(np.float32)[:, None]
@@ -208,7 +208,7 @@ def quantize_q2_k(x: np.ndarray) -> np.ndarray:
     lo = np.minimum(xb.min(-1), 0.0)
     hi = xb.max(-1)
     scale = (hi - lo) / 3
-    mins = -lo
+    mins = 0.0 - lo                                     # +0 (not -0) when lo is 0
     d = _f16(scale.max(-1) / 15.0)
     dmin = _f16(mins.max(-1) / 15.0)
     df = d.astype(np.float32)[:, None]
