@@ -288,18 +288,18 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
                 // per TMEM load; float(S) is exact (|S| <= 2^22 < 2^24).  (Ten warps put
                 // three on one SM sub-partition, whose 16K registers then allow 168 per thread.)
 #pragma unroll
-                for (int q8 = 0; q8 < 8; ++q8) {
-                    uint32_t r[16];
-                    tmem_ld_32x32b_x16(taddr + 16 * q8, r);
+                for (int q8 = 0; q8 < 16; ++q8) {
+                    uint32_t r[8];
+                    tmem_ld_32x32b_x8(taddr + 8 * q8, r);
                     tmem_wait_ld();
                     if (!live) continue;
 #pragma unroll
-                    for (int c4 = 0; c4 < 4; ++c4) {
-                        const float4 w = swp[4 * q8 + c4];
+                    for (int c4 = 0; c4 < 2; ++c4) {
+                        const float4 w = swp[2 * q8 + c4];
                         const float2 s0 = make_float2(__int2float_rn((int) r[4 * c4]), __int2float_rn((int) r[4 * c4 + 1]));
                         const float2 s1 = make_float2(__int2float_rn((int) r[4 * c4 + 2]), __int2float_rn((int) r[4 * c4 + 3]));
-                        f[8 * q8 + 2 * c4]     = __ffma2_rn(__fmul2_rn(s0, sx2), make_float2(w.x, w.y), f[8 * q8 + 2 * c4]);
-                        f[8 * q8 + 2 * c4 + 1] = __ffma2_rn(__fmul2_rn(s1, sx2), make_float2(w.z, w.w), f[8 * q8 + 2 * c4 + 1]);
+                        f[4 * q8 + 2 * c4]     = __ffma2_rn(__fmul2_rn(s0, sx2), make_float2(w.x, w.y), f[4 * q8 + 2 * c4]);
+                        f[4 * q8 + 2 * c4 + 1] = __ffma2_rn(__fmul2_rn(s1, sx2), make_float2(w.z, w.w), f[4 * q8 + 2 * c4 + 1]);
                     }
                 }
                 tc_fence_before();

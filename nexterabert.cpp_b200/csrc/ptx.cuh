@@ -162,6 +162,14 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)
         : "r"(taddr) : "memory");
 }
 
+// the same for 8 consecutive columns
+__device__ __forceinline__ void tmem_ld_32x32b_x8(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+        : "r"(taddr) : "memory");
+}
+
 // Shared-memory matrix descriptor for a K-major operand in the 128-byte swizzle
 // layout that a TMA SWIZZLE_128B load writes: rows of 128 bytes, 8-row atoms of
 // 1024 bytes (stride byte offset 1024), descriptor version 1 (sm_100).
