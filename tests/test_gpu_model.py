@@ -226,3 +226,26 @@ def test_float_encoder_files_are_refused_at_load(lib, capfd, preset):
     assert not h
     assert "is not a quantized matrix this build can expand to int8" in err
     assert "'blocks." in err
+
+
+@pytest.mark.parametrize("preset", ["Q4_K_M", "Q8_0"])
+def test_full_model_edge_lengths_match_reference(lib, reflib, preset):
+    """The full model on a batch of edge-case lengths against the reference compiled here:
+    1-token documents, lengths around the 8-key groups of the score lanes, around the band
+    half-width (128) and window (256), and around 2048, where the reference's attention switches to
+    blocked keys (src/nexterabert.cpp:776-780, :810-837)."""
+    path = sm.cached_model("full", sm.full_hparams(), preset, seed=0)
+    lens = np.array([1, 2, 7, 8, 9, 127, 129, 255, 256, 257, 2047, 2048, 2049], np.int32)
+    tok = sm.random_tokens(int(lens.sum()), 50368, seed=31)
+    m = Model(lib, path)
+    rc, hid, pooled = m.encode(tok, lens)
+    assert rc == 0
+    r = reflib.load(path, 0)
+    try:
+        wh, wp = reflib.encode(r, tok, lens)
+    finally:
+        reflib.L.nextera_free(r)
+    compare(hid, wh, f"hidden ({preset})")
+    compare(pooled, wp, f"pooled ({preset})")
+    print(f"{preset}: hidden bit-identical fraction {np.mean(hid == wh):.6f}")
+    m.close()
