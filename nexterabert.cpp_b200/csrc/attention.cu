@@ -377,8 +377,11 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
                                        : make_float4(0.f, 0.f, 0.f, 0.f);
             }
         };
-        kload(it.k0);
-        for (int kt = it.k0; kt < it.k1; kt += KT) {
+        // key tiles last to first: the maximum does not depend on the order, and pass 2 then starts
+        // on the scores written last, which are the likeliest to be still in L2
+        const int kt_last = it.k0 + (it.k1 - 1 - it.k0) / KT * KT;
+        kload(kt_last);
+        for (int kt = kt_last; kt >= it.k0; kt -= KT) {
             const int nk = min(KT, it.k1 - kt);
             __syncthreads();                                       // Ks free; Qs written
 #pragma unroll
@@ -390,7 +393,7 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
                 Ks[4 * d4 + 3][j] = kp[z].w;
             }
             __syncthreads();
-            if (kt + KT < it.k1) kload(kt + KT);
+            if (kt - KT >= it.k0) kload(kt - KT);
             // a warp whose 32 queries see none of its 16 keys (band layers) only stores zeros
             const bool live = kt + kb - 4 * (lane >> 3) < w_hi && kt + kb - 4 * (lane >> 3) + 16 > w_lo;
             float y0123[4][4], x45[4][4], x6[4][4], x01[4][4], x2[4][4], x0[4][4], x4[4][4];
