@@ -284,8 +284,8 @@ gemm_i8_tc(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUt
                 const float sxb = t < a.T ? sxs[row * a.n_blk + b] : 0.0f;
                 const float2 sx2 = make_float2(sxb, sxb);
                 const float4 * swp = (const float4 *) (sws + b * BN);
-                // f = fma(float(S) * sx, sw, f) per column, two columns per packed instruction, 16 columns
-                // per TMEM load; float(S) is exact (|S| <= 2^22 < 2^24).  (Ten warps put
+                // f = fma(float(S) * sx, sw, f) per column, two columns per packed instruction, 8 columns
+                // per TMEM load (16 spill at the register cap below); float(S) is exact (|S| <= 2^22 < 2^24).  (Ten warps put
                 // three on one SM sub-partition, whose 16K registers then allow 168 per thread.)
 #pragma unroll
                 for (int q8 = 0; q8 < 16; ++q8) {
