@@ -184,7 +184,8 @@ NEXTERA_API int32_t nextera_encode_partitioned(struct nextera_context * ctx, con
 /* Device-resident variant: d_tokens holds only this rank's sequences (those with
  * nextera_partition(...)[i] == rank, concatenated in batch order) in device memory; lengths is
  * the whole batch (host memory); rank 0's d_pooled (device, n_seqs x n_embd) receives every
- * sequence's pooled row in batch order.  Enqueued on `stream`; every rank must call it. */
+ * sequence's pooled row in batch order.  A rank that the partition gives no sequence may pass
+ * d_tokens = NULL.  Enqueued on `stream`; every rank must call it. */
 NEXTERA_API int32_t nextera_encode_partitioned_device(struct nextera_context * ctx, const int32_t * d_tokens,
                                                       const int32_t * lengths, int32_t n_seqs, float * d_pooled,
                                                       int32_t normalize, void * stream);

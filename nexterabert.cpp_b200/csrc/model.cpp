@@ -1824,13 +1824,14 @@ int32_t nextera_encode_partitioned(struct nextera_context * c, const int32_t * t
 
 int32_t nextera_encode_partitioned_device(struct nextera_context * c, const int32_t * d_tokens, const int32_t * lengths,
                                           int32_t n_seqs, float * d_pooled, int32_t normalize, void * stream) {
-    if (!c || !d_tokens) return 1;
+    if (!c) return 1;
     const int world = c->shard_comm ? c->shard_world : 1, rank = c->shard_comm ? c->shard_rank : 0;
     if (rank == 0 && !d_pooled) return 1;
     cudaSetDevice(c->device);
     PartPlan pp;
     int rc = make_part_plan(*c, lengths, n_seqs, rank, world, pp);
     if (rc) return rc;
+    if (!d_tokens && pp.my_tokens > 0) return 1;       // a rank given no sequences may pass NULL
     cudaStream_t s = (cudaStream_t) stream;
     rc = run_part(*c, pp, lengths, d_tokens, nullptr, false, normalize, s);
     if (rc) return rc;
