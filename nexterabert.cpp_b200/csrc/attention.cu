@@ -249,7 +249,9 @@ attn_kernel(const float * __restrict__ q, const float * __restrict__ k, const fl
 //           the other (dims l, 8 + l, ..., 56 + l), folding each finished lane
 //           into the full-group tree ((a0+a1)+(a2+a3)) + ((a4+a5)+(a6+a7)) as
 //           it completes.  Queries and keys sit transposed in shared memory
-//           ([dim][query], [dim][key]), so one float4 of each feeds 16 FMAs.
+//           ([dim][query], [dim][key]), so one float4 of each feeds 16 FMAs,
+//           issued as 8 packed f32x2 multiply-adds over diagonal pairs of the
+//           tile.
 //           Partial maxima over the keys in whole groups go to shared memory.
 //   pass 2  two threads per (query, head): the tail keys (the n % 8 after the
 //           last whole group) are recomputed with the hsum256 tree, then the
@@ -290,7 +292,7 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
     extern __shared__ __align__(16) float smem[];
     float (*Qs)[QT3] = reinterpret_cast<float (*)[QT3]>(smem);                       // [REP * D][QT3]
     float (*Ks)[KT] = reinterpret_cast<float (*)[KT]>(smem + REP * D * QT3);         // [D][KT]
-    float (*Vs)[D] = reinterpret_cast<float (*)[D]>(smem + REP * D * QT3 + D * KT);  // [KT][D]
+    // [KT][D] after Ks: only the rings of passes 2-3 use it (a 64-key pass-2 tile needs it)
     float (*Cw)[NQH] = reinterpret_cast<float (*)[NQH]>(smem + REP * D * QT3 + 2 * D * KT);   // [KT][NQH]
     float * mx = &Cw[0][0];                                        // [8][NQH], passes 1-2 only
     float * invs = smem + REP * D * QT3 + 2 * D * KT + KT * NQH;    // [NQH]
@@ -396,48 +398,62 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
             if (kt - KT >= it.k0) kload(kt - KT);
             // a warp whose 32 queries see none of its 16 keys (band layers) only stores zeros
             const bool live = kt + kb - 4 * (lane >> 3) < w_hi && kt + kb - 4 * (lane >> 3) + 16 > w_lo;
-            float y0123[4][4], x45[4][4], x6[4][4], x01[4][4], x2[4][4], x0[4][4], x4[4][4];
+            // The 4 x 4 tile in packed pairs, so that one f32x2 multiply-add advances two scores'
+            // chains (each half an IEEE fma, the same bits as two scalar ones): P[A][B][0] pairs
+            // q(2A).k(2B) with q(2A+1).k(2B+1), P[A][B][1] q(2A+1).k(2B) with q(2A).k(2B+1)
+            // (the query pair swapped in registers).  Score (a, b) is component b & 1 of
+            // P[a >> 1][b >> 1][(a ^ b) & 1].
+            float2 y0123[2][2][2], x45[2][2][2], x6[2][2][2], x01[2][2][2], x2[2][2][2], x0[2][2][2], x4[2][2][2];
 #pragma unroll
-            for (int a = 0; a < 4; ++a)
+            for (int A = 0; A < 2; ++A)
 #pragma unroll
-                for (int b2 = 0; b2 < 4; ++b2) x0[a][b2] = 0.0f;
+                for (int B = 0; B < 2; ++B)
+#pragma unroll
+                    for (int s2 = 0; s2 < 2; ++s2) x0[A][B][s2] = make_float2(0.0f, 0.0f);
             if (live) {
+            const float2 sc2 = make_float2(sc, sc);
 #pragma unroll
             for (int l = 0; l < 8; ++l) {
-                float acc[4][4];
+                float2 acc[2][2][2];
 #pragma unroll
                 for (int r = 0; r < 8; ++r) {
                     const int d = 8 * r + l;
                     const float4 qv = *(const float4 *) &Qh[d][qa];
                     const float4 kv = *(const float4 *) &Ks[d][kb];
-                    const float qq[4] = {qv.x, qv.y, qv.z, qv.w};
-                    const float kk[4] = {kv.x, kv.y, kv.z, kv.w};
+                    const float2 qp[2][2] = {{make_float2(qv.x, qv.y), make_float2(qv.y, qv.x)},
+                                             {make_float2(qv.z, qv.w), make_float2(qv.w, qv.z)}};
+                    const float2 kp2[2] = {make_float2(kv.x, kv.y), make_float2(kv.z, kv.w)};
 #pragma unroll
-                    for (int a = 0; a < 4; ++a)
+                    for (int A = 0; A < 2; ++A)
 #pragma unroll
-                        for (int b2 = 0; b2 < 4; ++b2)
-                            acc[a][b2] = r == 0 ? __fmul_rn(qq[a], kk[b2]) : __fmaf_rn(qq[a], kk[b2], acc[a][b2]);
+                        for (int B = 0; B < 2; ++B)
+#pragma unroll
+                            for (int s2 = 0; s2 < 2; ++s2)
+                                acc[A][B][s2] = r == 0 ? __fmul2_rn(qp[A][s2], kp2[B])
+                                                       : __ffma2_rn(qp[A][s2], kp2[B], acc[A][B][s2]);
                 }
 #pragma unroll
-                for (int a = 0; a < 4; ++a)
+                for (int A = 0; A < 2; ++A)
 #pragma unroll
-                    for (int b2 = 0; b2 < 4; ++b2) {
-                        const float c = acc[a][b2];
-                        switch (l) {
-                            case 0: x0[a][b2] = c; break;
-                            case 1: x01[a][b2] = __fadd_rn(x0[a][b2], c); break;
-                            case 2: x2[a][b2] = c; break;
-                            case 3: y0123[a][b2] = __fadd_rn(x01[a][b2], __fadd_rn(x2[a][b2], c)); break;
-                            case 4: x4[a][b2] = c; break;
-                            case 5: x45[a][b2] = __fadd_rn(x4[a][b2], c); break;
-                            case 6: x6[a][b2] = c; break;
-                            default: {
-                                const float s = __fmul_rn(__fadd_rn(y0123[a][b2],
-                                                                    __fadd_rn(x45[a][b2], __fadd_rn(x6[a][b2], c))), sc);
-                                x0[a][b2] = s;                     // the finished score
+                    for (int B = 0; B < 2; ++B)
+#pragma unroll
+                        for (int s2 = 0; s2 < 2; ++s2) {
+                            const float2 c = acc[A][B][s2];
+                            switch (l) {
+                                case 0: x0[A][B][s2] = c; break;
+                                case 1: x01[A][B][s2] = __fadd2_rn(x0[A][B][s2], c); break;
+                                case 2: x2[A][B][s2] = c; break;
+                                case 3: y0123[A][B][s2] = __fadd2_rn(x01[A][B][s2], __fadd2_rn(x2[A][B][s2], c)); break;
+                                case 4: x4[A][B][s2] = c; break;
+                                case 5: x45[A][B][s2] = __fadd2_rn(x4[A][B][s2], c); break;
+                                case 6: x6[A][B][s2] = c; break;
+                                default:                           // the finished score
+                                    x0[A][B][s2] = __fmul2_rn(__fadd2_rn(y0123[A][B][s2],
+                                                                         __fadd2_rn(x45[A][B][s2],
+                                                                                    __fadd2_rn(x6[A][B][s2], c))),
+                                                              sc2);
                             }
                         }
-                    }
             }
             }
             // stored: the score inside the query's key range, 0 outside (pass 3 reads them as weights)
@@ -448,9 +464,11 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
                     float sv[4];
 #pragma unroll
                     for (int a = 0; a < 4; ++a) {
+                        const float2 pr = x0[a >> 1][b2 >> 1][(a ^ b2) & 1];
+                        const float x = (b2 & 1) ? pr.y : pr.x;
                         const bool in = kj >= lo4[a] && kj < hi4[a];
-                        sv[a] = in ? x0[a][b2] : 0.0f;
-                        if (kj >= lo4[a] && kj < fe4[a]) ml[a] = (ml[a] < x0[a][b2]) ? x0[a][b2] : ml[a];
+                        sv[a] = in ? x : 0.0f;
+                        if (kj >= lo4[a] && kj < fe4[a]) ml[a] = (ml[a] < x) ? x : ml[a];
                     }
                     *(float4 *) (sc_base + (size_t) (kj - it.k0) * NQH + hq * QT3 + qa) =
                         make_float4(sv[0], sv[1], sv[2], sv[3]);
