@@ -368,34 +368,39 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
             }
         }
         const float (*Qh)[QT3] = Qs + hq * D;
-        // key tiles: the next tile's rows are loaded into registers while this one is used
+        // key tiles: the next tile's rows arrive by cp.async in the [KT][D] region that pass 1 does
+        // not otherwise use (row j's float4 d4 at j * D + 4 * (d4 ^ (j & 15)), so that the
+        // transposing reads below, 8 rows per phase, hit distinct banks) while this one is used
+        float * Kraw = smem + REP * D * QT3 + D * KT;
         constexpr int KPT = KT * D / 4 / NT;
-        float4 kp[KPT];
-        auto kload = [&](int kt) {
-#pragma unroll
-            for (int z = 0; z < KPT; ++z) {
-                const int i = tid + z * NT, j = i % KT, d4 = i / KT;
-                kp[z] = kt + j < it.k1 ? *(const float4 *) (kg + (ptrdiff_t) (kt + j) * D + 4 * d4)
-                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+        auto kissue = [&](int kt) {
+            for (int i = tid; i < KT * D / 4; i += NT) {
+                const int j = i / (D / 4), d4 = i % (D / 4);
+                float * dst = Kraw + j * D + 4 * (d4 ^ (j & 15));
+                if (kt + j < it.k1) cp_async16(dst, kg + (ptrdiff_t) (kt + j) * D + 4 * d4);
+                else *(float4 *) dst = make_float4(0.f, 0.f, 0.f, 0.f);
             }
+            cp_async_commit();
         };
         // key tiles last to first: the maximum does not depend on the order, and pass 2 then starts
         // on the scores written last, which are the likeliest to be still in L2
         const int kt_last = it.k0 + (it.k1 - 1 - it.k0) / KT * KT;
-        kload(kt_last);
+        kissue(kt_last);
         for (int kt = kt_last; kt >= it.k0; kt -= KT) {
             const int nk = min(KT, it.k1 - kt);
-            __syncthreads();                                       // Ks free; Qs written
+            cp_async_wait<0>();
+            __syncthreads();                                       // Kraw landed; Ks free; Qs written
 #pragma unroll
             for (int z = 0; z < KPT; ++z) {
                 const int i = tid + z * NT, j = i % KT, d4 = i / KT;
-                Ks[4 * d4 + 0][j] = kp[z].x;
-                Ks[4 * d4 + 1][j] = kp[z].y;
-                Ks[4 * d4 + 2][j] = kp[z].z;
-                Ks[4 * d4 + 3][j] = kp[z].w;
+                const float4 x = *(const float4 *) (Kraw + j * D + 4 * (d4 ^ (j & 15)));
+                Ks[4 * d4 + 0][j] = x.x;
+                Ks[4 * d4 + 1][j] = x.y;
+                Ks[4 * d4 + 2][j] = x.z;
+                Ks[4 * d4 + 3][j] = x.w;
             }
-            __syncthreads();
-            if (kt - KT >= it.k0) kload(kt - KT);
+            __syncthreads();                                       // Ks written; Kraw free
+            if (kt - KT >= it.k0) kissue(kt - KT);
             // a warp whose 32 queries see none of its 16 keys (band layers) only stores zeros
             const bool live = kt + kb - 4 * (lane >> 3) < w_hi && kt + kb - 4 * (lane >> 3) + 16 > w_lo;
             // The 4 x 4 tile in packed pairs, so that one f32x2 multiply-add advances two scores'
