@@ -250,8 +250,8 @@ attn_kernel(const float * __restrict__ q, const float * __restrict__ k, const fl
 //           into the full-group tree ((a0+a1)+(a2+a3)) + ((a4+a5)+(a6+a7)) as
 //           it completes.  Queries and keys sit transposed in shared memory
 //           ([dim][query], [dim][key]), so one float4 of each feeds 16 FMAs,
-//           issued as 8 packed f32x2 multiply-adds over diagonal pairs of the
-//           tile.
+//           issued as 8 packed f32x2 multiply-adds (one query against a key
+//           pair).
 //           Partial maxima over the keys in whole groups go to shared memory.
 //   pass 2  two threads per (query, head): the tail keys (the n % 8 after the
 //           last whole group) are recomputed with the hsum256 tree, then the
@@ -404,10 +404,9 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
             // a warp whose 32 queries see none of its 16 keys (band layers) only stores zeros
             const bool live = kt + kb - 4 * (lane >> 3) < w_hi && kt + kb - 4 * (lane >> 3) + 16 > w_lo;
             // The 4 x 4 tile in packed pairs, so that one f32x2 multiply-add advances two scores'
-            // chains (each half an IEEE fma, the same bits as two scalar ones): P[A][B][0] pairs
-            // q(2A).k(2B) with q(2A+1).k(2B+1), P[A][B][1] q(2A+1).k(2B) with q(2A).k(2B+1)
-            // (the query pair swapped in registers).  Score (a, b) is component b & 1 of
-            // P[a >> 1][b >> 1][(a ^ b) & 1].
+            // chains (each half an IEEE fma, the same bits as two scalar ones): P[A][B][s] holds
+            // query 2A + s against keys 2B and 2B + 1, the query's value in both halves.  Score
+            // (a, b) is component b & 1 of P[a >> 1][b >> 1][a & 1].
             float2 y0123[2][2][2], x45[2][2][2], x6[2][2][2], x01[2][2][2], x2[2][2][2], x0[2][2][2], x4[2][2][2];
 #pragma unroll
             for (int A = 0; A < 2; ++A)
@@ -425,8 +424,8 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
                     const int d = 8 * r + l;
                     const float4 qv = *(const float4 *) &Qh[d][qa];
                     const float4 kv = *(const float4 *) &Ks[d][kb];
-                    const float2 qp[2][2] = {{make_float2(qv.x, qv.y), make_float2(qv.y, qv.x)},
-                                             {make_float2(qv.z, qv.w), make_float2(qv.w, qv.z)}};
+                    const float2 qp[2][2] = {{make_float2(qv.x, qv.x), make_float2(qv.y, qv.y)},
+                                             {make_float2(qv.z, qv.z), make_float2(qv.w, qv.w)}};
                     const float2 kp2[2] = {make_float2(kv.x, kv.y), make_float2(kv.z, kv.w)};
 #pragma unroll
                     for (int A = 0; A < 2; ++A)
@@ -469,7 +468,7 @@ attn_tiled_kernel(const float * __restrict__ q, const float * __restrict__ k, co
                     float sv[4];
 #pragma unroll
                     for (int a = 0; a < 4; ++a) {
-                        const float2 pr = x0[a >> 1][b2 >> 1][(a ^ b2) & 1];
+                        const float2 pr = x0[a >> 1][b2 >> 1][a & 1];
                         const float x = (b2 & 1) ? pr.y : pr.x;
                         const bool in = kj >= lo4[a] && kj < hi4[a];
                         sv[a] = in ? x : 0.0f;
