@@ -262,14 +262,6 @@ attn_kernel(const float * __restrict__ q, const float * __restrict__ k, const fl
 //           zero outside a query's range (fma(0, v, o) leaves o unchanged).
 // ---------------------------------------------------------------------------
 
-// 16-byte asynchronous global -> shared copies (both addresses 16-byte aligned)
-__device__ __forceinline__ void cp_async16(void * dst, const void * src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
-                 :: "r"((uint32_t) __cvta_generic_to_shared(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
 
 template <int REP>
 constexpr int tiled_smem_floats() {

@@ -129,4 +129,13 @@ __device__ __forceinline__ float i2f_exact(int32_t s) {
     return __fsub_rn(__int_as_float(s + 0x4B400000), 12582912.0f);
 }
 
+// 16-byte asynchronous global -> shared copies (both addresses 16-byte aligned)
+__device__ __forceinline__ void cp_async16(void * dst, const void * src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                 :: "r"((uint32_t) __cvta_generic_to_shared(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
+
 } // namespace nxk

@@ -210,8 +210,10 @@ int launch_rows8(const Op & op, int T, int C, float * out, int8_t * q, float * s
 // ---------------------------------------------------------------------------
 // Depthwise convolutions along the tokens of a document, tiled: a block owns
 // CONV_ROWS rows x one 256-column block.  The rows it reads (its own plus k-1
-// of halo) are staged in shared memory once, as x (op_dwconv, :528-544) or as
-// the product a * x (op_lily_state, :548-579), with the taps; then each warp
+// of halo) are staged in shared memory once, as x (op_dwconv, :528-544: every
+// row of the tile by cp.async at once) or as the product a * x (op_lily_state,
+// :548-579: through registers, a few rows per thread at a time), with the taps;
+// each row's document bounds are looked up while the rows arrive; then each warp
 // runs the tap loop of its rows from shared memory in the reference's order
 // (taps ascending, only those inside the row's document) and emits the row's
 // block as fp32 or codes.
@@ -219,6 +221,7 @@ int launch_rows8(const Op & op, int T, int C, float * out, int8_t * q, float * s
 //   lily    v = 0;         v = fma(w[j], (a * x)[t + j - k/2], v);  v = v * b[t]
 // ---------------------------------------------------------------------------
 constexpr int CONV_ROWS = 32;
+static_assert(CONV_ROWS % 8 == 0, "the 8 warps of a block take the tile's rows in turn");
 constexpr int CONV_KMAX = 64;
 
 inline size_t conv_smem_bytes(int k) { return sizeof(float) * 256 * (size_t) (CONV_ROWS + 2 * k - 1); }
@@ -241,38 +244,63 @@ __global__ void __launch_bounds__(256) conv_kernel(const float * __restrict__ x,
     const int t0 = blockIdx.x * CONV_ROWS, cb = blockIdx.y * 256;
     const int ncol = min(256, C - cb);
     const int hk = k / 2;
-    // staged in batches of 3 items per thread, every load of a batch issued before its first use
-    for (int i0 = threadIdx.x; i0 < n_rows * 64; i0 += 3 * blockDim.x) {
-        float4 xv[3], av[3];
-        bool ok[3];
-#pragma unroll
-        for (int z = 0; z < 3; ++z) {
-            const int i = i0 + z * blockDim.x;
+    if (!LILY) {
+        for (int i = threadIdx.x; i < n_rows * 64; i += blockDim.x) {
             const int rr = i >> 6, c4 = i & 63;
             const int tr = t0 - hk + rr;
-            ok[z] = i < n_rows * 64 && tr >= -halo && tr < T + halo && 4 * c4 < ncol;   // rows that exist
-            if (ok[z]) {
-                const ptrdiff_t off = (ptrdiff_t) tr * C + cb + 4 * c4;
-                xv[z] = *(const float4 *) (x + off);
-                if (LILY) av[z] = *(const float4 *) (a + off);
-            }
+            if (tr >= -halo && tr < T + halo && 4 * c4 < ncol)     // rows that exist
+                cp_async16(P + 4 * i, x + (ptrdiff_t) tr * C + cb + 4 * c4);
         }
+        cp_async_commit();
+    }
+    // lane i < RPW: the taps of this warp's row i that lie inside the row's document, [j0, j1),
+    // as j0 | j1 << 8 (k <= 64)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int RPW = CONV_ROWS / 8;                          // rows per warp (256 threads)
+    static_assert(RPW <= 32, "one lane per row of the warp");
+    int jr = 0;
+    {
+        const int t = t0 + warp + 8 * lane;
+        if (lane < RPW && t < T) {
+            const int d = row_doc[t];
+            const int lo = doc_start[d], hi = lo + doc_len[d];
+            jr = max(0, lo - (t - hk)) | min(k, hi - (t - hk)) << 8;
+        }
+    }
+    // lily: staged in batches of 3 items per thread, every load of a batch issued before its first use
+    if (LILY) {
+        for (int i0 = threadIdx.x; i0 < n_rows * 64; i0 += 3 * blockDim.x) {
+            float4 xv[3], av[3];
+            bool ok[3];
 #pragma unroll
-        for (int z = 0; z < 3; ++z) {
-            if (!ok[z]) continue;
-            float4 p = xv[z];
-            if (LILY)
-                p = make_float4(__fmul_rn(av[z].x, p.x), __fmul_rn(av[z].y, p.y), __fmul_rn(av[z].z, p.z),
-                                __fmul_rn(av[z].w, p.w));
-            ((float4 *) P)[i0 + z * blockDim.x] = p;
+            for (int z = 0; z < 3; ++z) {
+                const int i = i0 + z * blockDim.x;
+                const int rr = i >> 6, c4 = i & 63;
+                const int tr = t0 - hk + rr;
+                ok[z] = i < n_rows * 64 && tr >= -halo && tr < T + halo && 4 * c4 < ncol;   // rows that exist
+                if (ok[z]) {
+                    const ptrdiff_t off = (ptrdiff_t) tr * C + cb + 4 * c4;
+                    xv[z] = *(const float4 *) (x + off);
+                    if (LILY) av[z] = *(const float4 *) (a + off);
+                }
+            }
+#pragma unroll
+            for (int z = 0; z < 3; ++z) {
+                if (!ok[z]) continue;
+                float4 p = xv[z];
+                if (LILY)
+                    p = make_float4(__fmul_rn(av[z].x, p.x), __fmul_rn(av[z].y, p.y), __fmul_rn(av[z].z, p.z),
+                                    __fmul_rn(av[z].w, p.w));
+                ((float4 *) P)[i0 + z * blockDim.x] = p;
+            }
         }
     }
     for (int i = threadIdx.x; i < k * 64; i += blockDim.x) {
         const int j = i >> 6, c4 = i & 63;
         if (4 * c4 < ncol) ((float4 *) W)[i] = *(const float4 *) (taps + (size_t) j * C + cb + 4 * c4);
     }
+    if (!LILY) cp_async_wait<0>();                             // this thread's copies have landed
     __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int c0 = 8 * lane;
     const bool on = c0 < ncol;
     const int n_blk = (C + I8_BLOCK - 1) / I8_BLOCK;
@@ -281,12 +309,11 @@ __global__ void __launch_bounds__(256) conv_kernel(const float * __restrict__ x,
 #pragma unroll
         for (int j = 0; j < (KS > 0 ? KS : 1); ++j) ld8(W + (size_t) j * 256 + c0, wr[j]);
     }
-    for (int rr = warp; rr < CONV_ROWS; rr += (int) (blockDim.x >> 5)) {
-        const int t = t0 + rr;
+    for (int i = 0; i < RPW; ++i) {
+        const int rr = warp + 8 * i, t = t0 + rr;
         if (t >= T) break;
-        const int d = row_doc[t];
-        const int lo = doc_start[d], hi = lo + doc_len[d];
-        const int j0 = max(0, lo - (t - hk)), j1 = min(k, hi - (t - hk));
+        const int jv = __shfl_sync(0xffffffffu, jr, i);
+        const int j0 = jv & 0xff, j1 = jv >> 8;
         float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         if (on) {
             float bv[8];
