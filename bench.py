@@ -110,6 +110,41 @@ def linear_ops(lengths) -> float:
     return 2.0 * macs
 
 
+def linear_floor_ms(lengths, peak_tops: float, hbm_gbs: float):
+    """Time floor of one step's int8 linears: per linear, the larger of its multiply-adds at the
+    tcgen05 rate and its HBM bytes at the measured copy rate.  Bytes per row: int8 codes in (K, plus
+    one fp32 scale per 256 inputs); out fp32 (4N), fp32 read and written again when the linear adds
+    into the residual (8N), or int8 codes and scales (c_fc's relu² epilogue).  Weights stay in L2
+    and are not counted.  Returns (floor ms, ms of the compute-bound linears, ms of the memory-bound)."""
+    C, I, H, G, D, r = 1024, 2304, 16, 8, 64, 64
+    T = float(np.sum(lengths))
+    nb = float(np.sum((lengths + 3) // 4))
+    import synth_model as sm
+    F32, RES, CODES = 0, 1, 2
+    lins = []                                    # (rows, K, N, output)
+    for bt in sm.FULL_BLOCKS:
+        if bt == "lily":
+            lins += [(T, C, r, F32), (T, C, r, F32), (T, r, C, F32), (T, C, C, F32), (T, C, C, F32),
+                     (T, C, C, RES)]
+        elif bt in ("swa", "attn"):
+            lins += [(T, C, H * D + 2 * G * D, F32), (T, H * D, C, F32), (T, C, C, RES)]
+        else:
+            lins += [(T, C, C, F32), (T, C, C, F32), (nb, C, H * D + 2 * G * D, F32), (T, C, C, F32),
+                     (T, C, C, F32), (T, C, C, RES)]
+        lins += [(T, C, I, CODES), (T, I, C, RES)]
+    floor = comp = mem = 0.0
+    for rows, K, N, kind in lins:
+        t_ops = 2.0 * rows * N * K / (peak_tops * 1e12)
+        out_b = {F32: 4.0 * N, RES: 8.0 * N, CODES: N + 4.0 * N / 256}[kind]
+        t_mem = rows * (K + 4.0 * K / 256 + out_b) / (hbm_gbs * 1e9)
+        floor += max(t_ops, t_mem)
+        if t_ops >= t_mem:
+            comp += t_ops
+        else:
+            mem += t_mem
+    return floor * 1e3, comp * 1e3, mem * 1e3
+
+
 def attention_work(lengths):
     """(fp32 FLOPs of scores + weighted values, algorithmic bytes of q/k/v/out) of one step."""
     H, G, D, half = 16, 8, 64, 128
@@ -622,6 +657,12 @@ def run_b200(args, rank, world, local_rank, dist):
                "library_source": "cuBLASLt dense int8 (torch._int_mm 8192^3) in this run",
                "algorithmic": "sum over the step's 141-per-token int8 linears of 2*T*N*K"}
         lin["frac"] = lin["achieved"] / lin["peak"]
+        fl, fl_c, fl_m = linear_floor_ms(lengths[mine], i8_peak, hbm_pk)
+        lin["floor_ms"] = fl
+        lin["frac_of_floor"] = fl / k_ms["int8_linear"]
+        lin["floor"] = (f"per linear the larger of its multiply-adds at the tcgen05 rate and its HBM bytes "
+                        f"(int8 codes in; fp32 out, residual read and written, or codes out) at {hbm_src}: "
+                        f"{fl_c:.1f} ms from compute-bound linears, {fl_m:.1f} ms from memory-bound ones")
         f32_peak = fp32_peak_tflops(torch)
         # the attention's arithmetic is fixed fp32 fused multiply-add chains in the reference's
         # order, which tensor cores cannot reproduce: its ceiling is the CUDA-core FMA pipe

@@ -125,3 +125,21 @@ def test_shard_id_exchange_gloo():
         if p.is_alive():
             p.kill()
     assert got[0] == got[1] and len(got[0]) == 128
+
+
+def test_bench_linear_floor_covers_the_counted_linears():
+    """bench.py's linear floor walks the same linears as its op count: with a memory rate so high
+    that every linear is compute-bound, the floor is the op count at the tcgen05 rate."""
+    import importlib.util
+    import numpy as np
+    spec = importlib.util.spec_from_file_location("bench_mod", ROOT / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    lengths = np.array([16, 17, 100, 511, 2048], dtype=np.int64)
+    peak = 4000.0
+    floor, comp, mem = bench.linear_floor_ms(lengths, peak, 1e12)
+    assert mem == 0.0 and abs(comp - floor) < 1e-12
+    assert abs(floor - bench.linear_ops(lengths) / (peak * 1e12) * 1e3) < 1e-9 * floor
+    # at the measured rates the fp32-output linears are memory-bound
+    floor2, comp2, mem2 = bench.linear_floor_ms(lengths, 4571.0, 6509.4)
+    assert mem2 > comp2 and floor2 > floor
