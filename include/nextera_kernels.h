@@ -115,6 +115,11 @@ NEXTERA_API int nxk_lily_state(const float * a, const float * x, const float * b
 NEXTERA_API int nxk_dwconv_halo(const float * x, const float * r, const float * taps, int k, int halo,
                                 const int32_t * row_doc, const int32_t * doc_start, const int32_t * doc_len,
                                 int T, int C, float * out, int8_t * q, float * sx, void * stream);
+/* nxk_dwconv_halo over inputs whose rows are ld floats apart (ld >= C, a multiple of 4): x and r may be
+ * column ranges of one wider matrix, e.g. two linears fused into one.  Outputs stay C wide. */
+NEXTERA_API int nxk_dwconv_halo_ld(const float * x, const float * r, int ld, const float * taps, int k, int halo,
+                                   const int32_t * row_doc, const int32_t * doc_start, const int32_t * doc_len,
+                                   int T, int C, float * out, int8_t * q, float * sx, void * stream);
 NEXTERA_API int nxk_lily_state_halo(const float * a, const float * x, const float * b, const float * taps, int k,
                                     int halo, const int32_t * row_doc, const int32_t * doc_start,
                                     const int32_t * doc_len, int T, int C, float * out, int8_t * q, float * sx,

@@ -45,6 +45,9 @@ constexpr int I8_BLOCK = 256;
 constexpr int HALO_ROWS = 8;
 // the load-time concatenation of an attention mixer's c_q, c_k and c_v (no such tensor in a file)
 const char * const QKV_NAME = "c_qkv.weight#fused";
+// Lily's in_proj and A: both read the layer's normalized input, so one linear computes both
+// (rows of in_proj, then of A) when the narrow convolution can read its two column ranges
+const char * const LTC_IN_NAME = "ltc_conv.in_A.weight#fused";
 
 struct hparams {
     int32_t n_vocab = 0, n_embd = 0, n_layer = 0, n_inter = 0, n_head = 0, n_kv_head = 0, head_dim = 0;
@@ -523,11 +526,23 @@ struct nextera_context * nextera_load(const char * path, struct nextera_params p
     }
 
     // attention mixers: c_q, c_k and c_v become one weight, rows in that order, so one GEMM
-    // computes all three projections
+    // computes all three projections; Lily mixers: in_proj and A the same way, when their rank is
+    // a width the narrow convolution takes (32, 64 or 128)
     const size_t n_file_linears = c->i8.size();
     for (int l = 0; l < hp.n_layer; ++l) {
-        if (hp.block_types[l] == MIX_LILY) continue;
         const std::string pre = "blocks." + std::to_string(l) + ".attn.";
+        if (hp.block_types[l] == MIX_LILY) {
+            auto ip = c->i8.find(pre + "ltc_conv.in_proj.weight"), ia = c->i8.find(pre + "ltc_conv.A.weight");
+            if (ip == c->i8.end() || ia == c->i8.end()) continue;
+            const int r = ip->second.n_out;
+            if (ia->second.n_out != r || ia->second.n_in != ip->second.n_in || (r != 32 && r != 64 && r != 128))
+                continue;
+            if (!fuse_rows(*c, {pre + "ltc_conv.in_proj.weight", pre + "ltc_conv.A.weight"}, pre + LTC_IN_NAME)) {
+                fprintf(stderr, "nexterabert: cannot build the fused in_proj/A weight of layer %d\n", l);
+                return nullptr;
+            }
+            continue;
+        }
         if (!fuse_rows(*c, {pre + "c_q.weight", pre + "c_k.weight", pre + "c_v.weight"}, pre + QKV_NAME)) {
             fprintf(stderr, "nexterabert: cannot build the fused q/k/v weight of layer %d\n", l);
             return nullptr;
@@ -1078,15 +1093,24 @@ int run_encoder(nextera_context & c, const Batch & b, float rope0_base, const in
         fw.mark(PROF_ROWS);
         fw.rows(nxk_rms_norm(X, fw.p(blk + "attn_norm.weight"), hp.rms_eps, T, C, nullptr, Q2, Q2s, s), "rms_norm");
         if (mt == MIX_LILY) {
-            const int r = fw.n_out(pre + "ltc_conv.in_proj.weight");
-            fw.linear(pre + "ltc_conv.in_proj.weight", Q2, Q2s, T, nullptr, Fa);
-            fw.linear(pre + "ltc_conv.A.weight", Q2, Q2s, T, nullptr, Fb);
+            const int r2 = fw.n_out(pre + LTC_IN_NAME);             // fused: in_proj | A, 2r columns
+            const int r = r2 > 0 ? r2 / 2 : fw.n_out(pre + "ltc_conv.in_proj.weight");
+            if (r2 > 0) {
+                fw.linear(pre + LTC_IN_NAME, Q2, Q2s, T, nullptr, Fa);
+            } else {
+                fw.linear(pre + "ltc_conv.in_proj.weight", Q2, Q2s, T, nullptr, Fa);
+                fw.linear(pre + "ltc_conv.A.weight", Q2, Q2s, T, nullptr, Fb);
+            }
             const ConvTaps * k1 = fw.taps(pre + "ltc_conv.kernel");
             if (!fw.ok) break;
             fw.mark(PROF_ROWS);
-            const int h1 = conv_halo(Fa, r, k1->k);
-            fw.rows(nxk_dwconv_halo(Fa, Fb, k1->taps.as<float>(), k1->k, h1, L.row_doc, L.start, L.len, T, r, nullptr,
-                                    Q1, Q1s, s), "dwconv");
+            const int h1 = conv_halo(Fa, r2 > 0 ? r2 : r, k1->k);
+            if (r2 > 0)
+                fw.rows(nxk_dwconv_halo_ld(Fa, Fa + r, r2, k1->taps.as<float>(), k1->k, h1, L.row_doc, L.start, L.len,
+                                           T, r, nullptr, Q1, Q1s, s), "dwconv");
+            else
+                fw.rows(nxk_dwconv_halo(Fa, Fb, k1->taps.as<float>(), k1->k, h1, L.row_doc, L.start, L.len, T, r,
+                                        nullptr, Q1, Q1s, s), "dwconv");
             fw.linear(pre + "ltc_conv.out_proj.weight", Q1, Q1s, T, nullptr, Fa);
             fw.linear(pre + "x_proj.weight", Q2, Q2s, T, nullptr, Fb);
             fw.linear(pre + "B_proj.weight", Q2, Q2s, T, nullptr, Fc);

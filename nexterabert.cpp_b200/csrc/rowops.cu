@@ -234,7 +234,7 @@ __global__ void __launch_bounds__(256) conv_kernel(const float * __restrict__ x,
                                                    const float * __restrict__ taps, int k, int halo,
                                                    const int32_t * __restrict__ row_doc,
                                                    const int32_t * __restrict__ doc_start,
-                                                   const int32_t * __restrict__ doc_len, int T, int C,
+                                                   const int32_t * __restrict__ doc_len, int T, int C, int ld,
                                                    float * __restrict__ out, int8_t * __restrict__ q,
                                                    float * __restrict__ sx) {
     extern __shared__ float4 conv_sm[];
@@ -249,7 +249,7 @@ __global__ void __launch_bounds__(256) conv_kernel(const float * __restrict__ x,
             const int rr = i >> 6, c4 = i & 63;
             const int tr = t0 - hk + rr;
             if (tr >= -halo && tr < T + halo && 4 * c4 < ncol)     // rows that exist
-                cp_async16(P + 4 * i, x + (ptrdiff_t) tr * C + cb + 4 * c4);
+                cp_async16(P + 4 * i, x + (ptrdiff_t) tr * ld + cb + 4 * c4);
         }
         cp_async_commit();
     }
@@ -279,7 +279,7 @@ __global__ void __launch_bounds__(256) conv_kernel(const float * __restrict__ x,
                 const int tr = t0 - hk + rr;
                 ok[z] = i < n_rows * 64 && tr >= -halo && tr < T + halo && 4 * c4 < ncol;   // rows that exist
                 if (ok[z]) {
-                    const ptrdiff_t off = (ptrdiff_t) tr * C + cb + 4 * c4;
+                    const ptrdiff_t off = (ptrdiff_t) tr * ld + cb + 4 * c4;
                     xv[z] = *(const float4 *) (x + off);
                     if (LILY) av[z] = *(const float4 *) (a + off);
                 }
@@ -318,7 +318,7 @@ __global__ void __launch_bounds__(256) conv_kernel(const float * __restrict__ x,
         if (on) {
             float bv[8];
             if (LILY) ld8(b + (size_t) t * C + cb + c0, bv);          // issued before the tap loop
-            if (!LILY && r) ld8(r + (size_t) t * C + cb + c0, v);
+            if (!LILY && r) ld8(r + (size_t) t * ld + cb + c0, v);
             if (KS > 0 && j0 == 0 && j1 == KS) {
 #pragma unroll
                 for (int j = 0; j < (KS > 0 ? KS : 1); ++j) {
@@ -355,7 +355,7 @@ __global__ void __launch_bounds__(256) conv_narrow_kernel(const float * __restri
                                                           const float * __restrict__ taps, int k, int halo,
                                                           const int32_t * __restrict__ row_doc,
                                                           const int32_t * __restrict__ doc_start,
-                                                          const int32_t * __restrict__ doc_len, int T,
+                                                          const int32_t * __restrict__ doc_len, int T, int ld,
                                                           float * __restrict__ out, int8_t * __restrict__ q,
                                                           float * __restrict__ sx) {
     constexpr int LPR = C / 8;                       // lanes per row
@@ -369,7 +369,7 @@ __global__ void __launch_bounds__(256) conv_narrow_kernel(const float * __restri
     for (int i = threadIdx.x; i < n4; i += blockDim.x) {
         const int rr = i / (C / 4), c4 = i % (C / 4);
         const int tr = t0 - hk + rr;
-        if (tr >= -halo && tr < T + halo) ((float4 *) P)[i] = *(const float4 *) (x + (ptrdiff_t) tr * C + 4 * c4);
+        if (tr >= -halo && tr < T + halo) ((float4 *) P)[i] = *(const float4 *) (x + (ptrdiff_t) tr * ld + 4 * c4);
     }
     for (int i = threadIdx.x; i < k * (C / 4); i += blockDim.x) ((float4 *) W)[i] = ((const float4 *) taps)[i];
     __syncthreads();
@@ -384,7 +384,7 @@ __global__ void __launch_bounds__(256) conv_narrow_kernel(const float * __restri
             const int d = row_doc[t];
             const int lo = doc_start[d], hi = lo + doc_len[d];
             const int j0 = max(0, lo - (t - hk)), j1 = min(k, hi - (t - hk));
-            if (r) ld8(r + (size_t) t * C + c0, v);
+            if (r) ld8(r + (size_t) t * ld + c0, v);
             for (int j = j0; j < j1; ++j) {
                 float pv[8], wv[8];
                 ld8(P + (size_t) (rr + j) * C + c0, pv);
@@ -416,11 +416,13 @@ __global__ void __launch_bounds__(256) conv_narrow_kernel(const float * __restri
     }
 }
 
+// ld: floats between the rows of x (and a, r) of the dwconv; the outputs and lily's inputs are C wide
 int launch_conv(bool lily, const float * x, const float * a, const float * r, const float * b, const float * taps,
                 int k, int halo, const int32_t * row_doc, const int32_t * doc_start, const int32_t * doc_len, int T,
-                int C, float * out, int8_t * q, float * sx, cudaStream_t s) {
+                int C, int ld, float * out, int8_t * q, float * sx, cudaStream_t s) {
     if (T < 0 || C <= 0 || (C & 31) || k <= 0 || k > CONV_KMAX || halo < 0 || (!q && !out) || (q && !sx))
         return NXK_EINVAL;
+    if (ld < C || (ld & 3) || (lily && ld != C)) return NXK_EINVAL;   // 16-byte row starts
     if (T == 0) return NXK_OK;
     if (!lily && (C == 32 || C == 64 || C == 128)) {
         auto narrow = [&](auto kern, int c) {
@@ -428,7 +430,7 @@ int launch_conv(bool lily, const float * x, const float * a, const float * r, co
             const size_t smem = sizeof(float) * (size_t) c * (size_t) (rows + 2 * k - 1);
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
             kern<<<(unsigned) ((T + rows - 1) / rows), 256, smem, s>>>(x, r, taps, k, halo, row_doc, doc_start,
-                                                                       doc_len, T, out, q, sx);
+                                                                       doc_len, T, ld, out, q, sx);
         };
         if (C == 32) narrow(conv_narrow_kernel<32>, 32);
         else if (C == 64) narrow(conv_narrow_kernel<64>, 64);
@@ -439,7 +441,7 @@ int launch_conv(bool lily, const float * x, const float * a, const float * r, co
     const size_t smem = conv_smem_bytes(k);
     auto go = [&](auto kern, const float * a_, const float * r_, const float * b_) {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
-        kern<<<grid, 256, smem, s>>>(x, a_, r_, b_, taps, k, halo, row_doc, doc_start, doc_len, T, C, out, q, sx);
+        kern<<<grid, 256, smem, s>>>(x, a_, r_, b_, taps, k, halo, row_doc, doc_start, doc_len, T, C, ld, out, q, sx);
     };
     if (lily) {
         if (k == 5) go(conv_kernel<true, 5>, a, nullptr, b);
@@ -767,27 +769,35 @@ int nxk_gate(const float * g, const float * y, int T, int C, float * out, int8_t
 int nxk_dwconv(const float * x, const float * r, const float * taps, int k, const int32_t * row_doc,
                const int32_t * doc_start, const int32_t * doc_len, int T, int C, float * out, int8_t * q,
                float * sx, void * stream) {
-    return launch_conv(false, x, nullptr, r, nullptr, taps, k, 0, row_doc, doc_start, doc_len, T, C, out, q, sx,
+    return launch_conv(false, x, nullptr, r, nullptr, taps, k, 0, row_doc, doc_start, doc_len, T, C, C, out, q, sx,
                        S(stream));
 }
 
 int nxk_dwconv_halo(const float * x, const float * r, const float * taps, int k, int halo, const int32_t * row_doc,
                     const int32_t * doc_start, const int32_t * doc_len, int T, int C, float * out, int8_t * q,
                     float * sx, void * stream) {
-    return launch_conv(false, x, nullptr, r, nullptr, taps, k, halo, row_doc, doc_start, doc_len, T, C, out, q, sx,
+    return launch_conv(false, x, nullptr, r, nullptr, taps, k, halo, row_doc, doc_start, doc_len, T, C, C, out, q, sx,
                        S(stream));
+}
+
+int nxk_dwconv_halo_ld(const float * x, const float * r, int ld, const float * taps, int k, int halo,
+                       const int32_t * row_doc, const int32_t * doc_start, const int32_t * doc_len, int T, int C,
+                       float * out, int8_t * q, float * sx, void * stream) {
+    return launch_conv(false, x, nullptr, r, nullptr, taps, k, halo, row_doc, doc_start, doc_len, T, C, ld, out, q,
+                       sx, S(stream));
 }
 
 int nxk_lily_state(const float * a, const float * x, const float * b, const float * taps, int k,
                    const int32_t * row_doc, const int32_t * doc_start, const int32_t * doc_len, int T, int C,
                    float * out, int8_t * q, float * sx, void * stream) {
-    return launch_conv(true, x, a, nullptr, b, taps, k, 0, row_doc, doc_start, doc_len, T, C, out, q, sx, S(stream));
+    return launch_conv(true, x, a, nullptr, b, taps, k, 0, row_doc, doc_start, doc_len, T, C, C, out, q, sx,
+                       S(stream));
 }
 
 int nxk_lily_state_halo(const float * a, const float * x, const float * b, const float * taps, int k, int halo,
                         const int32_t * row_doc, const int32_t * doc_start, const int32_t * doc_len, int T, int C,
                         float * out, int8_t * q, float * sx, void * stream) {
-    return launch_conv(true, x, a, nullptr, b, taps, k, halo, row_doc, doc_start, doc_len, T, C, out, q, sx,
+    return launch_conv(true, x, a, nullptr, b, taps, k, halo, row_doc, doc_start, doc_len, T, C, C, out, q, sx,
                        S(stream));
 }
 

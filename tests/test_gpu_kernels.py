@@ -6,6 +6,8 @@ follows the reference's order; its softmax tail exp is correctly rounded where
 the reference calls glibc's expf, so it must be within 1e-4 of the output's
 largest magnitude (the configuration's bar) and bit-identical almost everywhere.
 """
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -174,6 +176,15 @@ def test_conv_ops_bit_exact(ops, oracle, C, k):
     want = oracle.lily_state(x, r, b, taps, L)
     assert np.array_equal(ops.rows("nxk_lily_state", [P(dev(x)), P(dev(r)), P(dev(b)), P(dev(taps)), k, *lay, T, C],
                                    T, C, False), want)
+    # x and r as the two column ranges of one [T][2C] matrix, as the fused in_proj | A linear writes them
+    xr = dev(np.ascontiguousarray(np.concatenate([x, r], axis=1)))
+    px, pr = ctypes.c_void_p(xr.data_ptr()), ctypes.c_void_p(xr.data_ptr() + 4 * C)
+    args = [px, pr, 2 * C, P(dev(taps)), k, 0, *lay, T, C]
+    want = oracle.dwconv(x, r, taps, L)
+    assert np.array_equal(ops.rows("nxk_dwconv_halo_ld", args, T, C, False), want)
+    q, s = ops.rows("nxk_dwconv_halo_ld", args, T, C, True)
+    wq, ws = oracle.quantize_rows(want)
+    assert np.array_equal(q, wq) and np.array_equal(s, ws)
 
 
 def test_qk_prep_and_head_major_bit_exact(ops, oracle):
