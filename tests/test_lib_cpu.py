@@ -84,6 +84,12 @@ def test_kernel_layer_rejects_unsupported_shapes(built):
     assert L.nxk_rms_norm(None, None, 1e-8, 4, 100, None, None, None, None) == -1         # C not a multiple of 32
     assert L.nxk_attention(None, None, None, 4, 16, 2, 64, -1, None, None, None, None, 1, None, None,
                            None, 0, None, None) == -1                                     # 8 heads per KV head
+    # the strided dwconv: rows closer than C floats, or not 16-byte aligned (the output pointer is
+    # a placeholder; the checks reject the call before it is used)
+    fake = ctypes.c_void_p(256)
+    for ld in (60, 66):
+        assert L.nxk_dwconv_halo_ld(None, None, ld, None, 5, 0, None, None, None, 4, 64, fake, None, None,
+                                    None) == -1
 
 
 def test_shard_id_without_gpu():
