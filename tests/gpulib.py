@@ -59,6 +59,8 @@ def load_lib(path=None):
         "nxk_dwconv": ([vp, vp, vp, c_int, vp, vp, vp, c_int, c_int, vp, vp, vp, vp], c_int),
         "nxk_lily_state": ([vp, vp, vp, vp, c_int, vp, vp, vp, c_int, c_int, vp, vp, vp, vp], c_int),
         "nxk_dwconv_halo_ld": ([vp, vp, c_int, vp, c_int, c_int, vp, vp, vp, c_int, c_int, vp, vp, vp, vp], c_int),
+        "nxk_dwconv_halo": ([vp, vp, vp, c_int, c_int, vp, vp, vp, c_int, c_int, vp, vp, vp, vp], c_int),
+        "nxk_lily_state_halo": ([vp, vp, vp, vp, c_int, c_int, vp, vp, vp, c_int, c_int, vp, vp, vp, vp], c_int),
         "nxk_qk_prep": ([vp, vp, vp, vp, vp, vp, vp, c_int, c_int, c_int, c_int, vp, vp], c_int),
         "nxk_head_major": ([vp, c_int, c_int, c_int, vp, vp], c_int),
         "nxk_qkv_prep": ([vp, c_int, vp, vp, vp, vp, vp, vp, vp, vp, c_int, c_int, c_int, c_int, vp, vp, vp, vp],

@@ -187,6 +187,32 @@ def test_conv_ops_bit_exact(ops, oracle, C, k):
     assert np.array_equal(q, wq) and np.array_equal(s, ws)
 
 
+@pytest.mark.parametrize("C,k", [(64, 5), (256, 5), (128, 7)])
+def test_conv_halo_shard_bit_exact(ops, oracle, C, k):
+    """One shard of a longer document, as the sharded path runs it on one GPU: rows [off, off + T)
+    of a document of Ltot rows, the document starting before row 0 (start = -off) and the inputs
+    holding the halo rows around the shard; the outputs equal the whole document's rows."""
+    from gpulib import P, dev
+    Ltot, off, T = 300, 100, 100
+    h = k // 2
+    x, r, b, taps = cases.conv_case(C=C, k=k, seed=3 * C + k, lengths=np.array([Ltot], np.int32))
+    lay = [P(dev(np.zeros(T, np.int32))), P(dev(np.array([-off], np.int32))), P(dev(np.array([Ltot], np.int32)))]
+    dx, dr, db, dt = dev(x), dev(r), dev(b), dev(taps)
+    row = lambda t: ctypes.c_void_p(t.data_ptr() + 4 * off * t.shape[1])          # row `off` of a matrix
+    want = oracle.dwconv(x, r, taps, [Ltot])[off:off + T]
+    got = ops.rows("nxk_dwconv_halo", [row(dx), row(dr), P(dt), k, h, *lay, T, C], T, C, False)
+    assert np.array_equal(got, want)
+    # the strided entry point: x and r side by side in one [Ltot][2C] matrix
+    xr = dev(np.ascontiguousarray(np.concatenate([x, r], axis=1)))
+    px = ctypes.c_void_p(xr.data_ptr() + 4 * off * 2 * C)
+    got = ops.rows("nxk_dwconv_halo_ld", [px, ctypes.c_void_p(px.value + 4 * C), 2 * C, P(dt), k, h, *lay, T, C],
+                   T, C, False)
+    assert np.array_equal(got, want)
+    want = oracle.lily_state(x, r, b, taps, [Ltot])[off:off + T]
+    got = ops.rows("nxk_lily_state_halo", [row(dx), row(dr), row(db), P(dt), k, h, *lay, T, C], T, C, False)
+    assert np.array_equal(got, want)
+
+
 def test_qk_prep_and_head_major_bit_exact(ops, oracle):
     import torch
     from gpulib import P, dev, host
