@@ -69,6 +69,10 @@ def load_lib(path=None):
         "nxk_upsample_add": ([vp, vp, c_int, c_int, c_int, vp, vp, vp, vp, vp], c_int),
         "nxk_layer_norm": ([vp, vp, vp, c_float, c_int, c_int, vp, vp], c_int),
         "nxk_pool": ([vp, vp, vp, c_int, c_int, c_int, vp, vp], c_int),
+        "nxk_pool_continue": ([vp, c_int, c_int, vp, vp], c_int),
+        "nxk_pool_finish": ([c_int, c_int, c_int, vp, vp], c_int),
+        "nxk_attention_kv": ([vp, vp, vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int, vp, vp, vp, c_int, i32p, i32p,
+                              vp, c_size, vp, vp], c_int),
         "nxk_attention_workspace": ([i32p, c_int, c_int], c_size),
         "nxk_attention": ([vp, vp, vp, c_int, c_int, c_int, c_int, c_int, vp, vp, vp, vp, c_int, i32p, i32p,
                            vp, c_size, vp, vp], c_int),

@@ -334,6 +334,59 @@ def test_cfg2_attention(ops, oracle, half):
         assert float(np.mean(got[s0:s0 + n] == want)) >= 0.999, d
 
 
+@pytest.mark.parametrize("half", [8, -1])
+def test_attention_on_a_shard_matches_the_whole_document(ops, half):
+    """One shard of a long document on one GPU, as the sharded path runs it: query rows [off, off + T)
+    of a document of Ltot rows (off not a multiple of the 64-query tile), the document starting before
+    query row 0, with K / V gathered from the whole document (global: Tk = Ltot, koff = off) or a
+    halo-extended slice of it (band: Tk = T + 2 half, koff = half).  Bit-identical to the same rows of
+    the whole document through nxk_attention, which the tests above check against the oracle."""
+    import torch
+    from gpulib import P, dev, host
+    rng = np.random.default_rng(21)
+    H, G, D = 4, 2, 64
+    Ltot, off, T = 700, 250, 192
+    q = rng.standard_normal((Ltot, H * D)).astype(np.float32)
+    k = rng.standard_normal((G, Ltot, D)).astype(np.float32)
+    v = rng.standard_normal((G, Ltot, D)).astype(np.float32)
+    scale = np.full(1, 0.125, np.float32)
+    whole = run_attention(ops, q, k, v, H, G, half, scale, np.array([Ltot], np.int32))
+    if half < 0:
+        Tk, koff, ks, vs = Ltot, off, k, v
+    else:
+        Tk, koff = T + 2 * half, half
+        ks = np.ascontiguousarray(k[:, off - half:off + T + half])
+        vs = np.ascontiguousarray(v[:, off - half:off + T + half])
+    hs, hl = np.array([-off], np.int32), np.array([Ltot], np.int32)
+    i32 = ops.L.nxk_attention_kv.argtypes[14]
+    ws_bytes = int(ops.L.nxk_attention_workspace(hl.ctypes.data_as(i32), 1, half))
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device="cuda")
+    out = torch.empty((T, H * D), dtype=torch.float32, device="cuda")
+    dq, dk, dv = dev(np.ascontiguousarray(q[off:off + T])), dev(ks), dev(vs)
+    ops._ok(ops.L.nxk_attention_kv(P(dq), P(dk), P(dv), T, Tk, koff, H, G, D, half, P(dev(scale)), P(dev(hs)),
+                                   P(dev(hl)), 1, hs.ctypes.data_as(i32), hl.ctypes.data_as(i32), P(ws), ws.numel(),
+                                   P(out), None), "attention_kv")
+    assert np.array_equal(host(out), whole[off:off + T])
+
+
+def test_pool_over_shards_matches_the_whole(ops, oracle):
+    """The pooled sum carried over three shards in order (nxk_pool_continue), then nxk_pool_finish,
+    equals pooling the whole document, bit for bit."""
+    import torch
+    from gpulib import P, dev, host
+    rng = np.random.default_rng(12)
+    n, C = 300, 256
+    x = rng.standard_normal((n, C)).astype(np.float32)
+    dx = dev(x)
+    for normalize in (0, 1):
+        pooled = torch.zeros(C, dtype=torch.float32, device="cuda")
+        for a, b in ((0, 100), (100, 250), (250, n)):
+            ops._ok(ops.L.nxk_pool_continue(ctypes.c_void_p(dx.data_ptr() + 4 * a * C), b - a, C, P(pooled), None),
+                    "pool_continue")
+        ops._ok(ops.L.nxk_pool_finish(n, C, normalize, P(pooled), None), "pool_finish")
+        assert np.array_equal(host(pooled), oracle.pool(x, np.array([n], np.int32), normalize)[0])
+
+
 def test_layer_norm_and_pool(ops, oracle):
     import torch
     from gpulib import P, dev, host
