@@ -65,6 +65,8 @@ def load_lib(path=None):
         "nxk_head_major": ([vp, c_int, c_int, c_int, vp, vp], c_int),
         "nxk_qkv_prep": ([vp, c_int, vp, vp, vp, vp, vp, vp, vp, vp, c_int, c_int, c_int, c_int, vp, vp, vp, vp],
                          c_int),
+        "nxk_qkv_prep_kv": ([vp, c_int, vp, vp, vp, vp, vp, vp, vp, vp, c_int, c_int, c_int, c_int, c_int, c_int, vp, vp,
+                             vp, vp], c_int),
         "nxk_block_mean": ([vp, vp, c_int, c_int, vp, vp, vp, vp, c_int, vp, vp, vp, vp], c_int),
         "nxk_upsample_add": ([vp, vp, c_int, c_int, c_int, vp, vp, vp, vp, vp], c_int),
         "nxk_layer_norm": ([vp, vp, vp, c_float, c_int, c_int, vp, vp], c_int),

@@ -255,6 +255,19 @@ def test_qkv_prep_bit_exact(ops, oracle):
     assert np.array_equal(host(q), oracle.qk_prep(xq, qa, qb, base, L, H, D, 0))
     assert np.array_equal(host(k), oracle.qk_prep(xk, ka, kb, base, L, G, D, 1))
     assert np.array_equal(host(v), oracle.head_major(xv, G, D))
+    # the sharded layout: k and v at rows koff .. koff + T - 1 of buffers of Tk rows per head, the
+    # rows around them (halo or other shards' rows) left as they were
+    koff, Tk = 5, T + 9
+    q2 = torch.empty((T, H * D), dtype=torch.float32, device="cuda")
+    k2 = torch.full((G, Tk, D), 7.0, dtype=torch.float32, device="cuda")
+    v2 = torch.full((G, Tk, D), 7.0, dtype=torch.float32, device="cuda")
+    ops._ok(ops.L.nxk_qkv_prep_kv(P(dev(x)), x.shape[1], P(dev(qa)), P(dev(qb)), P(dev(ka)), P(dev(kb)), P(dev(c)),
+                                  P(dev(s)), P(dev(rd)), P(dev(start)), T, H, G, D, Tk, koff, P(q2), P(k2), P(v2),
+                                  None), "qkv_prep_kv")
+    assert np.array_equal(host(q2), host(q))
+    for got, want in ((host(k2), host(k)), (host(v2), host(v))):
+        assert np.array_equal(got[:, koff:koff + T], want)
+        assert np.all(got[:, :koff] == 7.0) and np.all(got[:, koff + T:] == 7.0)
 
 
 def test_hra_ops_bit_exact(ops, oracle):
